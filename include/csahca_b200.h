@@ -1,0 +1,141 @@
+/*
+ * csahca_b200 — C ABI of the B200 (sm_100a) compressed-sparse-attention decode kernels.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream
+ * (cudaStream_t passed as void*), enqueues its kernels on that stream and
+ * returns without synchronising.  Nothing here allocates device memory: outputs
+ * and workspaces are supplied by the caller.
+ *
+ * Return value: CSAHCA_OK (0) on success, otherwise a CSAHCA_E* code; the
+ * message of the last failure on the calling thread is csahca_last_error().
+ * Argument checks mirror the TORCH_CHECK conditions of the reference host code
+ * and return CSAHCA_EINVAL with the same message text.
+ *
+ * Reference: ypd666/CSAHCA (hybrid_attention/, csrc/).  Each declaration names
+ * the reference interface it replaces.
+ */
+#ifndef CSAHCA_B200_H_
+#define CSAHCA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+/* Element types of q / K / V / outputs. */
+#define CSAHCA_DTYPE_F32 0
+#define CSAHCA_DTYPE_F16 1
+#define CSAHCA_DTYPE_BF16 2
+
+/* Element types of CSA chunk-index tensors. */
+#define CSAHCA_INDEX_I32 0
+#define CSAHCA_INDEX_I64 1
+
+/* Status codes. */
+#define CSAHCA_OK 0
+#define CSAHCA_EINVAL 1       /* argument rejected (message in csahca_last_error) */
+#define CSAHCA_ECUDA 2        /* a CUDA runtime call failed */
+#define CSAHCA_EUNSUPPORTED 3 /* valid for the reference, not supported by these kernels */
+
+/* Message of the last non-zero status returned on the calling thread. */
+const char* csahca_last_error(void);
+
+/* Library version string. */
+const char* csahca_version(void);
+
+/*
+ * Reads and clears the device error word of the current device.  Kernels set it
+ * (instead of trapping) when a bounded wait gives up or a slot index falls
+ * outside its cache.  Synchronises the current device.  *code = 0 means no error.
+ */
+int csahca_read_device_error(int* code);
+
+/* ------------------------------------------------------------------ CSA scorer
+ * Chunk scorer + per-(batch, head) top-k.
+ * Replaces hybrid_attention/reference.py:40-56 (chunk_mean + select_topk_chunks),
+ * called by hybrid_attention/benchmark.py:97 and model_inference.py:53,183.
+ *
+ *   score[b,h,c] = (q[b,h,:] . mean_t K[b,h,c*chunk + t,:]) / sqrt(head_dim)   (fp32)
+ *   out[b,h,:]   = indices of the min(top_k, S/chunk) largest scores, largest
+ *                  first, equal scores ordered by lower chunk index.
+ *
+ * q [B,H,D], k_cache [B,H,S,D] of `dtype`; S % chunk_size == 0.
+ * seq_lens: NULL, or int32 [B] per-request valid lengths (each a multiple of
+ *   chunk_size, <= S).  Request b then only scores its first seq_lens[b]/chunk
+ *   chunks, and slots past that count are written as -1.
+ * out_indices: int32 [B,H,min(top_k, S/chunk_size)].
+ * workspace: csahca_csa_select_topk_workspace_size() bytes, zero-filled before
+ *   its first use; every call leaves it zero-filled again.  Calls that may run
+ *   concurrently must not share a workspace.
+ * head_dim in {32, 64, 128, 256, 512}.
+ */
+size_t csahca_csa_select_topk_workspace_size(int64_t batch, int64_t heads, int64_t seq_len, int64_t chunk_size);
+int csahca_csa_select_topk(const void* q, const void* k_cache, const int32_t* seq_lens, int dtype, int64_t batch,
+                           int64_t heads, int64_t seq_len, int64_t head_dim, int64_t chunk_size, int64_t top_k,
+                           int32_t* out_indices, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------ CSA decode
+ * Split-K decode over the selected chunks with an in-kernel log-sum-exp combine.
+ * Replaces csrc/csa_attention.cu:330-385 (csa_decode_forward_cuda) and
+ * csrc/csa_attention.cu:387-452 (csa_decode_forward_tiled_cuda), i.e. the
+ * pybind symbols csa_decode_forward / csa_decode_forward_tiled
+ * (csrc/bindings.cpp:54-77,158-160).
+ *
+ * q [B,H,D], k_cache / v_cache [B,H,S,D] of `dtype`, chunk_indices [B,H,top_k]
+ * (int32 or int64); out [B,H,D] of `dtype`.  Slots with a negative chunk index
+ * and tokens at or beyond S are skipped; a (b,h) with no token left gets zeros.
+ * The tile size of the reference is a tuning knob only and has no counterpart:
+ * results do not depend on it.
+ * workspace: csahca_csa_decode_workspace_size() bytes, same zero-fill contract
+ *   as the scorer's (a separate buffer).  head_dim in {32, 64, 128, 256, 512}.
+ */
+size_t csahca_csa_decode_workspace_size(int64_t batch, int64_t heads, int64_t head_dim, int64_t top_k,
+                                        int64_t chunk_size);
+int csahca_csa_decode(const void* q, const void* k_cache, const void* v_cache, const void* chunk_indices,
+                      int index_dtype, int dtype, int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim,
+                      int64_t top_k, int64_t chunk_size, void* out, void* workspace, size_t workspace_bytes,
+                      void* stream);
+
+/* ------------------------------------------------------------------ DSV4 decode
+ * DeepSeek-V4 paged FP8 latent-cache decode (compress ratio 0 / 4 / 128).
+ * Replaces csrc/dsv4_attention.cu:585-657 (dsv4_swa_decode_forward_cuda),
+ * :659-760 (dsv4_sparse_decode_forward_cuda) and :762-909
+ * (dsv4_decode_forward_tiled_cuda), i.e. the pybind symbols
+ * dsv4_swa_decode_forward / dsv4_sparse_decode_forward /
+ * dsv4_decode_forward_tiled (csrc/bindings.cpp:79-164).
+ *
+ * Cache rows: 448 e4m3 + 64 bf16 dims (576 bytes) at page*bytes_per_page +
+ * (loc%page_size)*576, UE8M0 scales at page*bytes_per_page + page_size*576 +
+ * (loc%page_size)*8, page = loc/page_size.
+ * q [Q,H,512] of q_dtype; out [Q,H,512] of q_dtype.
+ * token_indices int32 [Q,topk_slots]; topk_lengths NULL or int32 [Q] (clamped
+ * to [0,topk_slots]); the extra (compressed) cache arguments may be NULL /
+ * zero-sized.  Negative slot indices are skipped.  attn_sink NULL or fp32 [H]
+ * (a virtual token with score sink[h] and value 0).  The tile size of the
+ * reference is a tuning knob with no counterpart here.
+ * Slot indices at or beyond num_pages*page_size are skipped and flag the device
+ * error word (the reference reads out of bounds there).
+ */
+int csahca_dsv4_decode(const void* q, int q_dtype, int64_t num_queries, int64_t heads, const uint8_t* cache,
+                       int64_t num_pages, int64_t bytes_per_page, int64_t page_size, const int32_t* token_indices,
+                       int64_t topk_slots, const int32_t* topk_lengths, const uint8_t* extra_cache,
+                       int64_t extra_num_pages, int64_t extra_bytes_per_page, int64_t extra_page_size,
+                       const int32_t* extra_token_indices, int64_t extra_topk_slots,
+                       const int32_t* extra_topk_lengths, const float* attn_sink, float softmax_scale, void* out,
+                       void* stream);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CSAHCA_B200_H_ */
