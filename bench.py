@@ -1,0 +1,393 @@
+"""Benchmark of the CSA / DSV4 decode path on B200 (one process per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Default workload (the metric's batched case): one
+dynamic CSA decode step for a batch of 64 requests x 32 heads, head_dim 128,
+chunk 64, top-k 16, bf16, per-request context uniform over multiples of 64 in
+[4096, 32768].  A step = score every valid chunk of K and select the top-16
+per (request, head) (csa_select kernel), then split-K attention over the 16 x
+64 selected tokens (csa_decode kernel).  K/V (34 GB) are larger than L2, so no
+flush is needed between steps.  Multi-GPU: weak scaling, every rank decodes its
+own 64-request batch (different seed) with no collective on the data path;
+the step time is the max over ranks.
+
+At N=1 the line also carries ``secondary``: DSV4 decode (configs 4 and 5: C0,
+C4, C128) and config 1, each timed alone with CUDA events.
+
+``--impl reference`` times the reference's CPU implementation of the same step
+(the numpy port in ``oracle/``, one process per host core over requests) on
+rank 0 only and prints the same metric.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "CSA batched dynamic decode throughput (score+top-k+split-K attention), config 2"
+UNIT = "tokens/s"
+CONFIG = {"workload": "csa_batched_dynamic_decode (BASELINE config 2)", "batch": 64, "heads": 32,
+          "head_dim": 128, "max_seq_len": 32768, "min_seq_len": 4096, "chunk_size": 64, "top_k": 16,
+          "dtype": "bf16", "l2": "inputs (K/V 34 GB) larger than L2; no flush"}
+# DRAM bytes per launch from one ncu capture of each kernel (profiles/*.md), scaled to the
+# bench workload by units processed; None until captured.
+NCU_TRAFFIC = {"csa_select": None}
+
+
+def _peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------------------------------------- clocks
+REASONS = ["clocks_event_reasons.hw_slowdown", "clocks_event_reasons.hw_thermal_slowdown",
+           "clocks_event_reasons.sw_thermal_slowdown", "clocks_event_reasons.sw_power_cap"]
+
+
+class ClockSampler:
+    """nvidia-smi sampling (200 ms) of SM clock and throttle reasons while running."""
+
+    def __init__(self, index: int) -> None:
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+        self._t = None
+
+    def __enter__(self):
+        q = "clocks.sm,clocks.max.sm,power.draw," + ",".join(REASONS)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=lambda: self.lines.extend(iter(self.proc.stdout.readline, "")),
+                                       daemon=True)
+            self._t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            if self._t is not None:
+                self._t.join(timeout=2)
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], [], set()
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 3 + len(REASONS):
+                continue
+            try:
+                sm.append(float(f[0]))
+                mx.append(float(f[1]))
+            except ValueError:
+                continue
+            for name, val in zip(REASONS, f[3:]):
+                if val.lower().startswith("active"):
+                    reasons.add(name.split(".")[-1])
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        busy = [s for s in sm if s > 0.5 * max(sm)] or sm
+        return {"sm_mhz": float(np.median(busy)), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------------------- CPU oracle
+_CPU_SAMPLE = None
+
+
+def _cpu_request(i: int) -> int:
+    from oracle import csa
+
+    q, k, v, L, c, top_k = _CPU_SAMPLE[i]
+    sel = csa.select_topk_chunks(q, k, c, top_k, "bf16")
+    csa.csa_reference(q, k, v, chunk_size=c, top_k=top_k, dtype="bf16", selected_chunks=sel)
+    return 1
+
+
+def make_cpu_sample(n: int, seed: int = 0):
+    """``n`` config-2 requests generated on the host with the same distributions
+    (only each request's valid prefix is materialised)."""
+    g = torch.Generator().manual_seed(seed)
+    lens = torch.randint(4096 // 64, 32768 // 64 + 1, (n,), generator=g) * 64
+    out = []
+    for i in range(n):
+        L = int(lens[i])
+        q = torch.randn(1, 32, 128, generator=g).to(torch.bfloat16)
+        k = torch.randn(1, 32, L // 64, 64, 128, generator=g)
+        k += torch.randn(1, 32, L // 64, 1, 1, generator=g) * 0.5
+        k = k.view(1, 32, L, 128).to(torch.bfloat16)
+        v = torch.randn(1, 32, L, 128, generator=g).to(torch.bfloat16)
+        cv = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+        out.append((cv(q), cv(k), cv(v), L, 64, 16))
+    return out
+
+
+def time_cpu_oracle(sample, workers: int, repeats: int = 1) -> tuple[float, list[float]]:
+    """Requests decoded per second by the numpy port, ``workers`` processes over requests."""
+    global _CPU_SAMPLE
+    import concurrent.futures as cf
+    import multiprocessing as mp
+
+    from threadpoolctl import threadpool_limits
+
+    _CPU_SAMPLE = sample
+    times = []
+    with threadpool_limits(1), cf.ProcessPoolExecutor(workers, mp_context=mp.get_context("fork")) as ex:
+        list(ex.map(_cpu_request, range(min(len(sample), workers))))  # warm the workers
+        for _ in range(repeats):
+            t0 = time.perf_counter()
+            n = sum(ex.map(_cpu_request, range(len(sample))))
+            times.append(time.perf_counter() - t0)
+    return n / float(np.median(times)), times
+
+
+# ------------------------------------------------------------------------------------------- GPU arms
+def _event():
+    return torch.cuda.Event(enable_timing=True)
+
+
+def bench_csa(dev, rank: int, world: int, steps: int, warmup: int, secondary: bool) -> dict:
+    from csahca_b200 import extension as ext
+    from csahca_b200 import workloads as W
+
+    batch = W.csa_batched(dev, seed=1000 * rank)
+    nbytes = W.csa_algorithmic_bytes(batch)
+    q, k, v, lens, c, top_k = batch.q, batch.k, batch.v, batch.seq_lens, batch.chunk, batch.top_k
+    torch.cuda.synchronize(dev)
+
+    def step():
+        sel = ext.select_topk_chunks(q, k, c, top_k, lens)
+        return ext.csa_decode_forward_tiled(q, k, v, sel, c)
+
+    for _ in range(max(3, warmup)):
+        step()
+    ev = [(_event(), _event(), _event()) for _ in range(steps)]
+    _barrier(world)
+    torch.cuda.synchronize(dev)
+    with ClockSampler(dev.index) as clk:
+        t_start, t_end = _event(), _event()
+        t_start.record()
+        for e0, e1, e2 in ev:
+            e0.record()
+            sel = ext.select_topk_chunks(q, k, c, top_k, lens)
+            e1.record()
+            ext.csa_decode_forward_tiled(q, k, v, sel, c)
+            e2.record()
+        t_end.record()
+        torch.cuda.synchronize(dev)
+        # keep the sampler alive for at least a few samples
+        time.sleep(max(0.0, 0.5 - t_start.elapsed_time(t_end) / 1e3))
+    total_ms = t_start.elapsed_time(t_end)
+    sel_ms = sum(e0.elapsed_time(e1) for e0, e1, _ in ev) / steps
+    dec_ms = sum(e1.elapsed_time(e2) for _, e1, e2 in ev) / steps
+    total_ms = _max_over_ranks(total_ms, dev, world)
+    _barrier(world)
+
+    # end to end through the public API: pinned host q in, host output out
+    q_host = q.cpu().pin_memory()
+    out_host = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    for _ in range(3):
+        q.copy_(q_host, non_blocking=True)
+        out_host.copy_(step(), non_blocking=True)
+    torch.cuda.synchronize(dev)
+    _barrier(world)
+    e_s, e_e = _event(), _event()
+    e_s.record()
+    for _ in range(steps):
+        q.copy_(q_host, non_blocking=True)
+        out_host.copy_(step(), non_blocking=True)
+    e_e.record()
+    torch.cuda.synchronize(dev)
+    e2e_ms = _max_over_ranks(e_s.elapsed_time(e_e), dev, world)
+
+    hbm, peak_kind = _peaks()
+    achieved = nbytes["scorer"] / (sel_ms / 1e3) / 1e9
+    res = {
+        "total_ms": total_ms, "steps": steps, "select_ms": sel_ms, "decode_ms": dec_ms,
+        "e2e_ms": e2e_ms, "clocks": clk.summary(),
+        "h2d": q_host.numel() * q_host.element_size(), "d2h": out_host.numel() * out_host.element_size(),
+        "roofline": {"bound": "hbm", "kernel": "csa_select (chunk scorer + top-k)",
+                     "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 4), "peak_source": f"{peak_kind} hbm_gbs",
+                     "traffic": NCU_TRAFFIC["csa_select"],
+                     "algorithmic_bytes": nbytes["scorer"]},
+        "decode_kernel": {"achieved_gbs": round(nbytes["decode"] / (dec_ms / 1e3) / 1e9, 1),
+                          "frac": round(nbytes["decode"] / (dec_ms / 1e3) / 1e9 / hbm, 4),
+                          "algorithmic_bytes": nbytes["decode"]},
+        "step_gbs": round(nbytes["step"] / (total_ms / steps / 1e3) / 1e9, 1),
+    }
+    del batch, q, k, v
+    torch.cuda.empty_cache()
+    if secondary:
+        res["secondary"] = bench_secondary(dev, hbm)
+    return res
+
+
+def _time_kernel(fn, dev, iters=50, warm=5) -> float:
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize(dev)
+    a, b = _event(), _event()
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    torch.cuda.synchronize(dev)
+    return a.elapsed_time(b) / iters
+
+
+def bench_secondary(dev, hbm: float) -> dict:
+    from csahca_b200 import extension as ext
+    from csahca_b200 import workloads as W
+
+    out = {}
+    cases = {
+        "dsv4_c0 (config 4: Q128 H64 window 128, ctx 2048-16384)":
+            dict(num_queries=128, heads=64, context=(2048, 16384), ratio=0, window=128),
+        "dsv4_c4 (config 5: Q256 H64 ctx 65536, 512 + 64 C4 slots)":
+            dict(num_queries=256, heads=64, context=65536, ratio=4, n_main=512, n_extra=64),
+        "dsv4_c128 (config 5: Q256 H64 ctx 65536, 512 + 64 C128 slots)":
+            dict(num_queries=256, heads=64, context=65536, ratio=128, n_main=512, n_extra=64),
+    }
+    for name, kw in cases.items():
+        b = W.dsv4_cache(dev, **kw)
+        if b.extra_cache is not None:
+            fn = lambda b=b: ext.dsv4_sparse_decode_forward(  # noqa: E731
+                b.q, b.cache, b.token_indices, b.topk_lengths, b.extra_cache, b.extra_token_indices,
+                b.extra_topk_lengths, b.attn_sink, b.page_size, b.extra_page_size, b.softmax_scale)
+        else:
+            fn = lambda b=b: ext.dsv4_swa_decode_forward(  # noqa: E731
+                b.q, b.cache, b.token_indices, b.topk_lengths, b.attn_sink, b.page_size, b.softmax_scale)
+        ms = _time_kernel(fn, dev)
+        nb = W.dsv4_algorithmic_bytes(b)
+        slots = b.token_indices.shape[1] + (0 if b.extra_token_indices is None else b.extra_token_indices.shape[1])
+        flops = 4 * b.q.shape[0] * b.q.shape[1] * slots * 512
+        out[name] = {"us_per_step": round(ms * 1e3, 2), "tokens_per_s": round(b.q.shape[0] / (ms / 1e3), 1),
+                     "achieved_gbs": round(nb / (ms / 1e3) / 1e9, 1), "hbm_frac": round(nb / (ms / 1e3) / 1e9 / hbm, 4),
+                     "tensor_tflops": round(flops / (ms / 1e3) / 1e12, 1), "algorithmic_bytes": nb}
+        del b
+        torch.cuda.empty_cache()
+    # config 1: B1 H8 S32768 D128 c64 k8, one dynamic step
+    g = torch.Generator(device=dev).manual_seed(0)
+    q = torch.randn(1, 8, 128, generator=g, device=dev, dtype=torch.bfloat16)
+    k = torch.randn(1, 8, 32768, 128, generator=g, device=dev, dtype=torch.bfloat16)
+    v = torch.randn(1, 8, 32768, 128, generator=g, device=dev, dtype=torch.bfloat16)
+    ms = _time_kernel(lambda: ext.csa_decode_step(q, k, v, 64, 8), dev, iters=200)
+    sel = ext.select_topk_chunks(q, k, 64, 8)
+    ms_dec = _time_kernel(lambda: ext.csa_decode_forward_tiled(q, k, v, sel, 64, 8), dev, iters=200)
+    out["csa_cfg1 (config 1: B1 H8 S32768 k8)"] = {
+        "us_per_step_dynamic": round(ms * 1e3, 2), "us_decode_precomputed": round(ms_dec * 1e3, 2),
+        "decode_gbs_selected_kv": round(8 * 512 * 128 * 2 * 2 / (ms_dec / 1e3) / 1e9, 1)}
+    return out
+
+
+def _barrier(world: int) -> None:
+    if world > 1:
+        torch.distributed.barrier()
+
+
+def _max_over_ranks(x: float, dev, world: int) -> float:
+    if world <= 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------------------------------- main
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-secondary", action="store_true")
+    ap.add_argument("--cpu-requests", type=int, default=8, help="requests in one CPU-oracle sample")
+    a = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    cores = os.cpu_count() or 1
+
+    if a.impl == "reference":
+        if rank != 0:
+            return 0
+        workers = max(1, min(cores, a.cpu_requests))
+        sample = make_cpu_sample(a.cpu_requests)
+        steps = max(1, a.steps)
+        value, times = time_cpu_oracle(sample, workers, repeats=steps)
+        line = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "impl": "reference", "n_gpus": a.gpus,
+                "steps": steps, "warmup": a.warmup, "ms_per_step": round(1e3 * float(np.median(times)), 2),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (seeded, config-2 distributions)", "config": CONFIG,
+                "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": workers, "kind": "port",
+                                 "sample": f"{len(sample)} config-2 requests x 32 heads per step (numpy port of "
+                                           "reference.py select_topk_chunks + csa_reference), one process per "
+                                           "request"},
+                "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return 0
+
+    if world > 1:
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    r = bench_csa(dev, rank, world, a.steps, a.warmup, secondary=(world == 1 and not a.no_secondary))
+    if rank == 0:
+        ms = r["total_ms"] / a.steps
+        value = world * 64 / (ms / 1e3)
+        e2e_ms = r["e2e_ms"] / a.steps
+        line = {"metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": a.steps,
+                "warmup": a.warmup, "ms_per_step": round(ms, 4), "us_per_step": round(ms * 1e3, 1),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (seeded, config-2 distributions; no dataset exists for this path)",
+                "config": dict(CONFIG, parallelism=f"request-sharded x{world}, no collective"),
+                "gpu_launches": 2 * a.steps,
+                "kernel_ms": {"csa_select": round(r["select_ms"], 4), "csa_decode": round(r["decode_ms"], 4)},
+                "step_achieved_gbs": r["step_gbs"], "roofline": r["roofline"], "decode_kernel": r["decode_kernel"],
+                "e2e": {"value": round(world * 64 / (e2e_ms / 1e3), 1), "unit": UNIT,
+                        "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]},
+                "clocks": r["clocks"]}
+        if "secondary" in r:
+            line["secondary"] = r["secondary"]
+        if world == 1:
+            workers = max(1, min(cores, a.cpu_requests))
+            sample = make_cpu_sample(a.cpu_requests)
+            cpu_v, _ = time_cpu_oracle(sample, workers)
+            line["cpu_baseline"] = {"value": round(cpu_v, 3), "unit": UNIT, "cores": workers, "kind": "port",
+                                    "sample": f"{len(sample)} config-2 requests x 32 heads (numpy port of "
+                                              "select_topk_chunks + csa_reference), one process per request"}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
