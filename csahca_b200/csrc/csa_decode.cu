@@ -19,6 +19,7 @@
 //   [0, 4*BH) arrival counters (rounded up to 256 B), then fp32 partials
 //   [BH][U][D+2] = (acc[D], max, sum).
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -325,4 +326,74 @@ extern "C" int csahca_csa_decode(const void* q, const void* k_cache, const void*
     case CSAHCA_DTYPE_F32: return dispatch_decode_dim<float>(head_dim, p, rows, index_dtype, s);
     default: return csahca_set_arg_error("unsupported dtype");
   }
+}
+
+// ---------------------------------------------------------------------------------------------------
+// Allocation-free variant of csahca_csa_decode.
+//
+// Some callers cannot hand us a workspace: a serving process that reserved all
+// of HBM for its KV cache at start-up and forbids later cudaMalloc calls, code
+// that must not trigger cudaMalloc's implicit device synchronisation in a
+// latency-critical loop, or a foreign-language binding with no device
+// allocator of its own.  This entry point keeps its scratch (the row arrival
+// counters and the split partials) in a fixed array owned by the library, so
+// the caller passes only inputs and outputs and no call allocates anything.
+//
+// Limits and rules:
+//   * the array is 8 MiB and exists on every GPU that loads the library, until
+//     the process exits; problems needing more scratch are rejected;
+//   * the first call on a device looks the array's device address up
+//     (cudaGetSymbolAddress) with that device current; make that first call
+//     before any stream capture;
+//   * all calls share the one array and it keeps the previous call's contents:
+//     each call clears the counters it needs at zero on its own stream, and two
+//     calls whose kernels overlap on the GPU (different streams, or different
+//     host threads without ordering) race on it.
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB on every device that loads the library
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {};
+
+// Device address of g_noalloc_scratch on the current device (looked up once per device;
+// the name itself is only a host-side stand-in and must never reach a kernel).
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  CSAHCA_RETURN_IF_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return csahca_set_unsupported("device index out of range");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    CSAHCA_RETURN_IF_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return CSAHCA_OK;
+}
+
+}  // namespace
+
+extern "C" size_t csahca_csa_decode_noalloc_max_scratch_bytes(void) { return kNoAllocScratchBytes; }
+
+extern "C" int csahca_csa_decode_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                                         const void* chunk_indices, int index_dtype, int dtype, int64_t batch,
+                                         int64_t heads, int64_t seq_len, int64_t head_dim, int64_t top_k,
+                                         int64_t chunk_size, void* out, void* stream) {
+  if (batch < 0 || heads < 0 || top_k < 0) return csahca_set_arg_error("sizes must be non-negative");
+  const size_t need = csahca_csa_decode_workspace_size(batch, heads, head_dim, top_k, chunk_size);
+  if (need > kNoAllocScratchBytes)
+    return csahca_set_arg_error(
+        "csahca_csa_decode_noalloc: this problem needs more scratch than the library's fixed 8 MiB buffer; "
+        "use csahca_csa_decode with a caller-provided workspace");
+  void* scratch = nullptr;
+  const int st = noalloc_scratch(&scratch);
+  if (st != CSAHCA_OK) return st;
+  // The counters must start at zero; clear them on the caller's stream (no allocation).
+  const int64_t rows = batch * heads;
+  if (rows > 0)
+    CSAHCA_RETURN_IF_CUDA(cudaMemsetAsync(scratch, 0, align256(size_t(rows) * 4), static_cast<cudaStream_t>(stream)));
+  return csahca_csa_decode(q, k_cache, v_cache, chunk_indices, index_dtype, dtype, batch, heads, seq_len, head_dim,
+                           top_k, chunk_size, out, scratch, kNoAllocScratchBytes, stream);
 }

@@ -102,6 +102,23 @@ int csahca_csa_decode(const void* q, const void* k_cache, const void* v_cache, c
                       int64_t top_k, int64_t chunk_size, void* out, void* workspace, size_t workspace_bytes,
                       void* stream);
 
+/*
+ * Allocation-free CSA decode (no counterpart in the reference).
+ * Same computation and arguments as csahca_csa_decode minus the workspace: the
+ * scratch is a fixed 8 MiB array inside the library (one per GPU, held until
+ * process exit), for callers that cannot allocate device memory at call time --
+ * e.g. a server that pre-reserved all HBM, a latency-critical loop that must
+ * avoid cudaMalloc's implicit synchronisation, or a foreign-language binding
+ * without a device allocator.  Problems whose scratch would exceed
+ * csahca_csa_decode_noalloc_max_scratch_bytes() return CSAHCA_EINVAL.  The first
+ * call on a device resolves the array's device address; make it before any
+ * stream capture.  All calls share the array: calls that overlap on the GPU race.
+ */
+size_t csahca_csa_decode_noalloc_max_scratch_bytes(void);
+int csahca_csa_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, const void* chunk_indices,
+                              int index_dtype, int dtype, int64_t batch, int64_t heads, int64_t seq_len,
+                              int64_t head_dim, int64_t top_k, int64_t chunk_size, void* out, void* stream);
+
 /* ------------------------------------------------------------------ DSV4 decode
  * DeepSeek-V4 paged FP8 latent-cache decode (compress ratio 0 / 4 / 128).
  * Replaces csrc/dsv4_attention.cu:585-657 (dsv4_swa_decode_forward_cuda),
