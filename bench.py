@@ -260,37 +260,47 @@ def _time_kernel(fn, dev, iters=50, warm=5) -> float:
     return a.elapsed_time(b) / iters
 
 
+DSV4_CASES = {
+    "dsv4_c0 (config 4: Q128 H64 window 128, ctx 2048-16384)":
+        dict(num_queries=128, heads=64, context=(2048, 16384), ratio=0, window=128),
+    "dsv4_c4 (config 5: Q256 H64 ctx 65536, 512 + 64 C4 slots)":
+        dict(num_queries=256, heads=64, context=65536, ratio=4, n_main=512, n_extra=64),
+    "dsv4_c128 (config 5: Q256 H64 ctx 65536, 512 + 64 C128 slots)":
+        dict(num_queries=256, heads=64, context=65536, ratio=128, n_main=512, n_extra=64),
+}
+
+
+def bench_dsv4_case(dev, hbm: float, kw: dict, iters: int = 50, warm: int = 5) -> dict:
+    from csahca_b200 import extension as ext
+    from csahca_b200 import workloads as W
+
+    b = W.dsv4_cache(dev, **kw)
+    if b.extra_cache is not None:
+        fn = lambda: ext.dsv4_sparse_decode_forward(  # noqa: E731
+            b.q, b.cache, b.token_indices, b.topk_lengths, b.extra_cache, b.extra_token_indices,
+            b.extra_topk_lengths, b.attn_sink, b.page_size, b.extra_page_size, b.softmax_scale)
+    else:
+        fn = lambda: ext.dsv4_swa_decode_forward(  # noqa: E731
+            b.q, b.cache, b.token_indices, b.topk_lengths, b.attn_sink, b.page_size, b.softmax_scale)
+    ms = _time_kernel(fn, dev, iters=iters, warm=warm)
+    nb = W.dsv4_algorithmic_bytes(b)
+    slots = b.token_indices.shape[1] + (0 if b.extra_token_indices is None else b.extra_token_indices.shape[1])
+    flops = 4 * b.q.shape[0] * b.q.shape[1] * slots * 512
+    res = {"us_per_step": round(ms * 1e3, 2), "tokens_per_s": round(b.q.shape[0] / (ms / 1e3), 1),
+           "achieved_gbs": round(nb / (ms / 1e3) / 1e9, 1), "hbm_frac": round(nb / (ms / 1e3) / 1e9 / hbm, 4),
+           "tensor_tflops": round(flops / (ms / 1e3) / 1e12, 1), "algorithmic_bytes": nb}
+    del b
+    torch.cuda.empty_cache()
+    return res
+
+
 def bench_secondary(dev, hbm: float) -> dict:
     from csahca_b200 import extension as ext
     from csahca_b200 import workloads as W
 
     out = {}
-    cases = {
-        "dsv4_c0 (config 4: Q128 H64 window 128, ctx 2048-16384)":
-            dict(num_queries=128, heads=64, context=(2048, 16384), ratio=0, window=128),
-        "dsv4_c4 (config 5: Q256 H64 ctx 65536, 512 + 64 C4 slots)":
-            dict(num_queries=256, heads=64, context=65536, ratio=4, n_main=512, n_extra=64),
-        "dsv4_c128 (config 5: Q256 H64 ctx 65536, 512 + 64 C128 slots)":
-            dict(num_queries=256, heads=64, context=65536, ratio=128, n_main=512, n_extra=64),
-    }
-    for name, kw in cases.items():
-        b = W.dsv4_cache(dev, **kw)
-        if b.extra_cache is not None:
-            fn = lambda b=b: ext.dsv4_sparse_decode_forward(  # noqa: E731
-                b.q, b.cache, b.token_indices, b.topk_lengths, b.extra_cache, b.extra_token_indices,
-                b.extra_topk_lengths, b.attn_sink, b.page_size, b.extra_page_size, b.softmax_scale)
-        else:
-            fn = lambda b=b: ext.dsv4_swa_decode_forward(  # noqa: E731
-                b.q, b.cache, b.token_indices, b.topk_lengths, b.attn_sink, b.page_size, b.softmax_scale)
-        ms = _time_kernel(fn, dev)
-        nb = W.dsv4_algorithmic_bytes(b)
-        slots = b.token_indices.shape[1] + (0 if b.extra_token_indices is None else b.extra_token_indices.shape[1])
-        flops = 4 * b.q.shape[0] * b.q.shape[1] * slots * 512
-        out[name] = {"us_per_step": round(ms * 1e3, 2), "tokens_per_s": round(b.q.shape[0] / (ms / 1e3), 1),
-                     "achieved_gbs": round(nb / (ms / 1e3) / 1e9, 1), "hbm_frac": round(nb / (ms / 1e3) / 1e9 / hbm, 4),
-                     "tensor_tflops": round(flops / (ms / 1e3) / 1e12, 1), "algorithmic_bytes": nb}
-        del b
-        torch.cuda.empty_cache()
+    for name, kw in DSV4_CASES.items():
+        out[name] = bench_dsv4_case(dev, hbm, kw)
     # config 1: B1 H8 S32768 D128 c64 k8, one dynamic step
     g = torch.Generator(device=dev).manual_seed(0)
     q = torch.randn(1, 8, 128, generator=g, device=dev, dtype=torch.bfloat16)
@@ -327,6 +337,10 @@ def main() -> int:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--cpu-requests", type=int, default=8, help="requests in one CPU-oracle sample")
+    ap.add_argument("--workload", choices=["csa_batched", "dsv4_c0", "dsv4_c4", "dsv4_c128"], default="csa_batched",
+                    help="dsv4_*: time only that DSV4 case (profiling / diagnosis); prints kernel timings")
+    ap.add_argument("--queries", type=int, default=0, help="dsv4_*: override the number of queries")
+    ap.add_argument("--context", type=int, default=0, help="dsv4_c4/c128: override the per-request context")
     a = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -358,6 +372,15 @@ def main() -> int:
         torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local))
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    if a.workload != "csa_batched":
+        kw = dict(next(v for k, v in DSV4_CASES.items() if k.startswith(a.workload)))
+        if a.queries:
+            kw["num_queries"] = a.queries
+        if a.context and kw["ratio"]:
+            kw["context"] = a.context
+        res = bench_dsv4_case(dev, _peaks()[0], kw, iters=a.steps, warm=max(3, a.warmup))
+        print(json.dumps({"workload": a.workload, "config": {k: str(v) for k, v in kw.items()}, **res}), flush=True)
+        return 0
     r = bench_csa(dev, rank, world, a.steps, a.warmup, secondary=(world == 1 and not a.no_secondary))
     if rank == 0:
         ms = r["total_ms"] / a.steps

@@ -36,6 +36,7 @@
 // Every wait on an mbarrier is bounded; on a timeout the CTA raises an abort
 // flag, records kErrWaitTimeout in the device error word and all roles leave.
 #include <algorithm>
+#include <type_traits>
 
 #include "common.cuh"
 #include "sm100.cuh"
@@ -50,30 +51,51 @@ constexpr int kRope = 64;
 constexpr int kDim = kNope + kRope;           // 512
 constexpr int kRowBytes = kNope + 2 * kRope;  // 576 data bytes per slot
 constexpr int kScaleBytes = 8;                // 7 UE8M0 scales + 1 pad per slot
-constexpr int kSlots = 128;                   // slots per block (MMA M of S^T)
+constexpr int kSlots = 64;                    // slots per block (MMA M of S^T)
 constexpr int kHeads = 64;                    // heads per CTA item (MMA N)
 
 constexpr int kSoftWarps = 4;
 constexpr int kMmaWarp = 4;
 constexpr int kProdWarp0 = 5;
-constexpr int kProdWarps = 8;
+constexpr int kProdWarps = 11;
 constexpr int kProdThreads = kProdWarps * 32;
-constexpr int kThreads = (kProdWarp0 + kProdWarps) * 32;  // 416
+constexpr int kThreads = (kProdWarp0 + kProdWarps) * 32;  // 512 (4 warps per sub-partition, 128 registers)
 
-constexpr uint32_t kQBytes = kHeads * kDim * 2;     // 65536
-constexpr uint32_t kSubTileBytes = kSlots * 128;    // 16384
-constexpr uint32_t kPairBytes = 2 * kSubTileBytes;  // 32768
-constexpr uint32_t kPBytes = kSlots * kHeads * 2;   // 16384
+constexpr int kKBufs = 2;                             // K tiles (and S / P buffers) in flight
+constexpr uint32_t kQBytes = kHeads * kDim * 2;      // 65536
+constexpr uint32_t kSubTileBytes = kSlots * 128;     // 8192: 64 slot rows x 64 dims bf16
+constexpr uint32_t kPairBytes = 2 * kSubTileBytes;   // 16384: dims 128m .. 128m+127
+constexpr uint32_t kBlockBytes = 4 * kPairBytes;     // 65536: one block's K tile
+constexpr uint32_t kPBytes = kSlots * kHeads * 2;    // 8192 per buffer
 constexpr uint32_t kOffQ = 0;
 constexpr uint32_t kOffK = kOffQ + kQBytes;
-constexpr uint32_t kOffP = kOffK + 4 * kPairBytes;
-constexpr uint32_t kOffBar = kOffP + kPBytes;
-constexpr uint32_t kSmemBytes = kOffBar + 2048 + 1024;  // + barriers/scratch + alignment slack
+constexpr uint32_t kOffP = kOffK + kKBufs * kBlockBytes;
+constexpr uint32_t kOffBar = kOffP + kKBufs * kPBytes;
+constexpr int kTabBufs = 5;                                  // slot tables in flight (see producers)
+constexpr uint32_t kOffTab = kOffBar + 2048;
+constexpr uint32_t kTabBytes = kTabBufs * kSlots * 16;      // 5 KB
+constexpr uint32_t kSmemBytes = kOffTab + kTabBytes + 1024;  // + alignment slack
+static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemS = 256;
+constexpr uint32_t kTmemS = 256;  // S^T buffers at columns 256 and 320
+constexpr uint32_t kTmemL = 384;  // per-lane running sums of P per head (64 columns)
 
-constexpr uint32_t kIdescQK = idesc_bf16_f32(128, kHeads, 0, 0);
+// Optional stage timestamps of CTA 0 (build with -DCSAHCA_DSV4_TRACE; diagnosis only).
+#ifdef CSAHCA_DSV4_TRACE
+__device__ long long g_dsv4_trace[2 * 8 * 16];
+#define DSV4_TRACE(item_no, blk, ev)                                                      \
+  do {                                                                                    \
+    if (blockIdx.x == 0 && (item_no) < 2 && (blk) < 8)                                    \
+      g_dsv4_trace[((item_no) * 8 + (blk)) * 16 + (ev)] = clock64();                      \
+  } while (0)
+#else
+#define DSV4_TRACE(item_no, blk, ev) \
+  do {                               \
+  } while (0)
+#endif
+
+constexpr uint32_t kIdescQK = idesc_bf16_f32(kSlots, kHeads, 0, 0);
 constexpr uint32_t kIdescPV = idesc_bf16_f32(128, kHeads, 1, 1);
 
 struct Dsv4Params {
@@ -98,12 +120,11 @@ struct Dsv4Params {
 // Barrier / scratch area (after the P buffer).
 struct Bars {
   uint64_t q_full, q_empty;
-  uint64_t k_full[4], k_empty[4];
-  uint64_t s_full, p_full, o_full, o_empty;
+  uint64_t k_full[kKBufs][4], k_empty[kKBufs][4];
+  uint64_t s_full[kKBufs], p_full[kKBufs];
+  uint64_t o_full, o_empty, pv_done;
   uint32_t tmem_base;
   int abort_flag;
-  int any_rescale;
-  int pad;
   float red[kSoftWarps][kHeads];  // per-warp column partials
   float m_use[kHeads];            // running max (log2 domain) used for P
   float alpha[kHeads];            // O/l rescale factors of the current block
@@ -131,34 +152,124 @@ __device__ __forceinline__ SlotSpace slot_space(const Dsv4Params& p, int q) {
   return s;
 }
 
-struct SlotRef {
-  const uint8_t* data;   // 576-byte row
-  const uint8_t* scale;  // 8 scale bytes
+// Producer work items of a block: (slot, 16-byte chunk) pairs grouped by K pair
+// m (dims 128m..128m+127): pairs 0-2 hold nope chunks 8m..8m+7 (8 per slot),
+// pair 3 holds nope chunks 24-27 and the 8 rope chunks (12 per slot).
+// Thread ptid takes items ptid, ptid + kProdThreads, ... of each pair.
+__host__ __device__ constexpr int pair_chunks(int m) { return m < 3 ? 8 : 12; }
+__host__ __device__ constexpr int pair_items(int m) { return kSlots * pair_chunks(m); }
+__host__ __device__ constexpr int per_thread(int m) { return (pair_items(m) + kProdThreads - 1) / kProdThreads; }
+__host__ __device__ constexpr int item_off(int m) { return m == 0 ? 0 : item_off(m - 1) + per_thread(m - 1); }
+// Producer threads 0..kSlots-1 also resolve the slot tables (one slot each); -1 for the rest.
+__device__ __forceinline__ int resolver_id(int ptid) { return ptid < kSlots ? ptid : -1; }
+constexpr int kItemsPerThread = item_off(3) + per_thread(3);
+
+// One resolved slot of a block: its 576-byte row (nullptr = skipped) and its 8 scale bytes.
+struct SlotEntry {
+  const uint8_t* row;
+  uint2 scales;
+};
+static_assert(sizeof(SlotEntry) == 16, "slot table entry is 16 bytes");
+
+// Threads 0..127 of the producer group each resolve one slot of block `blk` of
+// query q into `tab` (index load, 32-bit page arithmetic, scale-byte load).
+__device__ __forceinline__ void resolve_block(const Dsv4Params& p, const SlotSpace& sp, int q, int blk, int tid,
+                                              SlotEntry* tab) {
+  if (tid < 0 || tid >= kSlots) return;
+  SlotEntry e;
+  e.row = nullptr;
+  e.scales = make_uint2(0, 0);
+  const int gs = blk * kSlots + tid;
+  if (gs < sp.total()) {
+    const bool main = gs < sp.len_main;
+    const int loc = main ? __ldg(p.idx + size_t(q) * p.nmain + gs)
+                         : __ldg(p.xidx + size_t(q) * p.nextra + (gs - sp.len_main));
+    const int64_t cap = main ? p.capacity : p.xcapacity;
+    if (loc >= 0 && loc < cap) {
+      const unsigned page_size = unsigned(main ? p.page : p.xpage);
+      const unsigned page = unsigned(loc) / page_size;
+      const unsigned in_page = unsigned(loc) - page * page_size;
+      const uint8_t* pb = (main ? p.cache : p.xcache) + int64_t(page) * (main ? p.bpp : p.xbpp);
+      e.row = pb + int64_t(in_page) * kRowBytes;
+      e.scales = __ldg(reinterpret_cast<const uint2*>(pb + int64_t(page_size) * kRowBytes + int64_t(in_page) * kScaleBytes));
+    } else if (loc >= cap) {
+      report_device_error(p.err, kErrSlotOutOfRange);
+    }
+  }
+  tab[tid] = e;
+}
+
+// Split form of resolve_block for the producer pipeline: slot_loc() issues the
+// index load, finish_slot() turns the index into the row address and issues
+// the scale-byte load; the caller stores the entry one step later.
+struct PendingSlot {
+  int loc;
+  bool main;
 };
 
-// Resolve slot `gs` of query q to its row in a cache; false for skipped slots.
-__device__ __forceinline__ bool resolve_slot(const Dsv4Params& p, const SlotSpace& sp, int q, int gs, SlotRef& r,
-                                             bool report) {
-  if (gs >= sp.total()) return false;
-  const bool main = gs < sp.len_main;
-  const int loc = main ? __ldg(p.idx + size_t(q) * p.nmain + gs)
-                       : __ldg(p.xidx + size_t(q) * p.nextra + (gs - sp.len_main));
-  if (loc < 0) return false;
-  const int64_t cap = main ? p.capacity : p.xcapacity;
-  if (loc >= cap) {
-    if (report) report_device_error(p.err, kErrSlotOutOfRange);
-    return false;
+__device__ __forceinline__ PendingSlot slot_loc(const Dsv4Params& p, const SlotSpace& sp, int q, int blk, int tid) {
+  PendingSlot r;
+  r.loc = -1;
+  r.main = true;
+  const int gs = blk * kSlots + tid;
+  if (tid >= 0 && tid < kSlots && gs < sp.total()) {
+    r.main = gs < sp.len_main;
+    r.loc = r.main ? __ldg(p.idx + size_t(q) * p.nmain + gs) : __ldg(p.xidx + size_t(q) * p.nextra + (gs - sp.len_main));
   }
-  const int page_size = main ? p.page : p.xpage;
-  const int64_t bpp = main ? p.bpp : p.xbpp;
-  const uint8_t* base = main ? p.cache : p.xcache;
-  const int64_t page = loc / page_size;
-  const int in_page = int(loc - page * page_size);
-  const uint8_t* pb = base + page * bpp;
-  r.data = pb + int64_t(in_page) * kRowBytes;
-  r.scale = pb + int64_t(page_size) * kRowBytes + int64_t(in_page) * kScaleBytes;
-  return true;
+  return r;
 }
+
+__device__ __forceinline__ SlotEntry finish_slot(const Dsv4Params& p, const PendingSlot& ps) {
+  SlotEntry e;
+  e.row = nullptr;
+  e.scales = make_uint2(0, 0);
+  const int64_t cap = ps.main ? p.capacity : p.xcapacity;
+  if (ps.loc >= 0 && ps.loc < cap) {
+    const unsigned page_size = unsigned(ps.main ? p.page : p.xpage);
+    const unsigned page = unsigned(ps.loc) / page_size;
+    const unsigned in_page = unsigned(ps.loc) - page * page_size;
+    const uint8_t* pb = (ps.main ? p.cache : p.xcache) + int64_t(page) * (ps.main ? p.bpp : p.xbpp);
+    e.row = pb + int64_t(in_page) * kRowBytes;
+    e.scales = __ldg(reinterpret_cast<const uint2*>(pb + int64_t(page_size) * kRowBytes + int64_t(in_page) * kScaleBytes));
+    // Pull the row into L2 now (two blocks ahead of its register loads): the
+    // gather is latency-bound, and this keeps many rows in flight without
+    // registers or shared memory.
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(e.row), "r"(uint32_t(kRowBytes)) : "memory");
+  } else if (ps.loc >= cap) {
+    report_device_error(p.err, kErrSlotOutOfRange);
+  }
+  return e;
+}
+
+__device__ __forceinline__ int scale_byte(const uint2& s, int group) {
+  const uint32_t w = group < 4 ? s.x : s.y;
+  return int((w >> (8 * (group & 3))) & 0xFFu);
+}
+
+// Next (item, block) this CTA works on after (item, blk); false when none is left.
+__device__ __forceinline__ bool next_work(const Dsv4Params& p, int item, int blk, int nblk, int& nitem, int& nblk_out,
+                                          SlotSpace& nsp) {
+  if (blk + 1 < nblk) {
+    nitem = item;
+    nblk_out = blk + 1;
+    nsp = slot_space(p, item / p.groups);
+    return true;
+  }
+  for (int it = item + gridDim.x; it < p.num_items; it += gridDim.x) {
+    nsp = slot_space(p, it / p.groups);
+    if (nsp.blocks() > 0) {
+      nitem = it;
+      nblk_out = 0;
+      return true;
+    }
+  }
+  return false;
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 // 16 e4m3 bytes x 2^(s-127) -> 16 bf16 (exact).  The e4m3 exponent/mantissa
 // bits are placed into a bf16 pattern (value x 2^-120, subnormals included) and
@@ -177,6 +288,7 @@ __device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
 }
 
 __device__ __forceinline__ void dequant16(const uint4& raw, int scale_u8, uint4& lo, uint4& hi) {
+
   const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
   uint32_t o[8];
   if (scale_u8 <= 134) {
@@ -291,18 +403,139 @@ __device__ __forceinline__ float2 warp_colreduce64(float* v) {
   return make_float2(v[0], v[1]);
 }
 
-// Barrier of the 128 softmax threads that also ANDs a predicate across them.
-__device__ __forceinline__ bool soft_sync_and(bool ok) {
+// Named barrier `id` over `n` threads that also ANDs a predicate across them, so
+// a group leaves together when any member's bounded wait gave up.
+__device__ __forceinline__ bool group_sync_and(int id, int n, bool ok) {
   uint32_t r;
   asm volatile(
       "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.and.pred q, 1, 128, p;\n\t"
+      "setp.ne.u32 p, %3, 0;\n\t"
+      "bar.red.and.pred q, %1, %2, p;\n\t"
       "selp.u32 %0, 1, 0, q;\n\t}"
       : "=r"(r)
-      : "r"(uint32_t(ok))
+      : "r"(id), "r"(n), "r"(uint32_t(ok))
       : "memory");
   return r != 0;
+}
+__device__ __forceinline__ bool soft_sync_and(bool ok) { return group_sync_and(1, 128, ok); }
+
+__device__ __forceinline__ bool group_sync_or(int id, int n, bool x) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %3, 0;\n\t"
+      "bar.red.or.pred q, %1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(id), "r"(n), "r"(uint32_t(x))
+      : "memory");
+  return r != 0;
+}
+
+// 2^x with the hardware approximation (about 2 ulp; inputs here are <= 8).
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Two adjacent output elements (4 or 8 bytes, aligned) in one store.
+__device__ __forceinline__ void store_pair(__nv_bfloat16* dst, float a, float b) {
+  *reinterpret_cast<__nv_bfloat162*>(dst) = __floats2bfloat162_rn(a, b);
+}
+__device__ __forceinline__ void store_pair(__half* dst, float a, float b) {
+  *reinterpret_cast<__half2*>(dst) = __floats2half2_rn(a, b);
+}
+__device__ __forceinline__ void store_pair(float* dst, float a, float b) {
+  *reinterpret_cast<float2*>(dst) = make_float2(a, b);
+}
+
+// Loads / stores of one K pair's items for this producer thread (M is a
+// compile-time pair index so raw[] / scl[] stay in registers).
+template <int M>
+__device__ __forceinline__ void load_pair_items(const SlotEntry* tab, int ptid, uint4* raw, int* scl) {
+#pragma unroll
+  for (int k = 0; k < per_thread(M); ++k) {
+    const int i = ptid + kProdThreads * k;
+    const int n = item_off(M) + k;
+    raw[n] = make_uint4(0, 0, 0, 0);
+    scl[n] = -1;
+    if (i < pair_items(M)) {
+      const int c = 8 * M + i % pair_chunks(M);
+      const SlotEntry e = tab[i / pair_chunks(M)];
+      if (e.row) {
+        raw[n] = ldg_stream(e.row + c * 16);
+        scl[n] = c < 28 ? scale_byte(e.scales, c >> 2) : 0;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void load_block_items(const SlotEntry* tab, int ptid, uint4* raw, int* scl) {
+  load_pair_items<0>(tab, ptid, raw, scl);
+  load_pair_items<1>(tab, ptid, raw, scl);
+  load_pair_items<2>(tab, ptid, raw, scl);
+  load_pair_items<3>(tab, ptid, raw, scl);
+}
+
+template <int M>
+__device__ __forceinline__ void store_pair_items(uint32_t kbuf, int ptid, const uint4* raw, const int* scl) {
+#pragma unroll
+  for (int k = 0; k < per_thread(M); ++k) {
+    const int i = ptid + kProdThreads * k;
+    if (i < pair_items(M)) {
+      const int slot = i / pair_chunks(M), c = 8 * M + i % pair_chunks(M);
+      const int n = item_off(M) + k;
+      if (scl[n] >= 0)
+        store_k_chunk(kbuf, slot, c, raw[n], scl[n]);
+      else
+        zero_k_chunk(kbuf, slot, c);
+    }
+  }
+}
+
+// Position in the CTA's sequence of (item, block) work units; empty items are skipped.
+struct Cursor {
+  bool valid;
+  int item, blk, nblk;
+  SlotSpace sp;
+};
+
+__device__ __forceinline__ Cursor first_cursor(const Dsv4Params& p) {
+  Cursor c;
+  c.valid = false;
+  for (int it = blockIdx.x; it < p.num_items; it += gridDim.x) {
+    const SlotSpace sp = slot_space(p, it / p.groups);
+    if (sp.blocks() > 0) {
+      c.valid = true;
+      c.item = it;
+      c.blk = 0;
+      c.nblk = sp.blocks();
+      c.sp = sp;
+      break;
+    }
+  }
+  return c;
+}
+
+__device__ __forceinline__ Cursor next_cursor(const Dsv4Params& p, const Cursor& c) {
+  Cursor n = c;
+  if (!c.valid) return n;
+  if (c.blk + 1 < c.nblk) {  // same item: no memory access
+    n.blk = c.blk + 1;
+    return n;
+  }
+  n.valid = false;
+  int ni, nb;
+  SlotSpace nsp;
+  if (next_work(p, c.item, c.blk, c.nblk, ni, nb, nsp)) {
+    n.valid = true;
+    n.item = ni;
+    n.blk = nb;
+    n.nblk = nsp.blocks();
+    n.sp = nsp;
+  }
+  return n;
 }
 
 template <typename QT>
@@ -313,22 +546,25 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
   const uint32_t q_base = smem_u32(smem + kOffQ);
   const uint32_t k_base = smem_u32(smem + kOffK);
   const uint32_t p_base = smem_u32(smem + kOffP);
+  SlotEntry* tabs = reinterpret_cast<SlotEntry*>(smem + kOffTab);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   volatile int* abort_flag = &bars->abort_flag;
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, kProdThreads);
     mbar_init(&bars->q_empty, 1);
-    for (int m = 0; m < 4; ++m) {
-      mbar_init(&bars->k_full[m], kProdThreads);
-      mbar_init(&bars->k_empty[m], 1);
+    for (int b = 0; b < kKBufs; ++b) {
+      for (int m = 0; m < 4; ++m) {
+        mbar_init(&bars->k_full[b][m], kProdThreads);
+        mbar_init(&bars->k_empty[b][m], 1);
+      }
+      mbar_init(&bars->s_full[b], 1);
+      mbar_init(&bars->p_full[b], kSoftWarps * 32);
     }
-    mbar_init(&bars->s_full, 1);
-    mbar_init(&bars->p_full, kSoftWarps * 32);
     mbar_init(&bars->o_full, 1);
     mbar_init(&bars->o_empty, kSoftWarps * 32);
+    mbar_init(&bars->pv_done, 1);
     bars->abort_flag = 0;
-    bars->any_rescale = 0;
     fence_mbar_init();
   }
   if (threadIdx.x < kHeads) bars->m_use[threadIdx.x] = -INFINITY;
@@ -341,181 +577,235 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
 
   if (warp >= kProdWarp0) {
     // ------------------------------------------------------------ producers
+    // Block g goes to K buffer g%2.  One register set, rotated pair by pair:
+    // right after the stores of pair m of block g, the loads of pair m of block
+    // g+1 go out into the same registers, so each row is in flight for about a
+    // block period before it is dequantised.  Slot tables are resolved two
+    // blocks ahead (index loads two steps ahead, row address and scale-byte load
+    // one step ahead, table write at the start of a step) into
+    // tabs[g % kTabBufs]; table g is read by the loads of block g (during block
+    // g-1) and by the softmax of block g, which finishes before PV(g), i.e. before
+    // the stores of block g+2 complete; it is rewritten for block g+5 in step g+3.
     const int ptid = threadIdx.x - kProdWarp0 * 32;
-    uint32_t items_done = 0, blocks_done = 0;
-    for (int item = blockIdx.x; item < p.num_items; item += gridDim.x) {
-      const int q = item / p.groups, hg = item - q * p.groups;
-      const SlotSpace sp = slot_space(p, q);
-      const int nblk = sp.blocks();
-      if (nblk == 0) continue;
-      if (items_done > 0 && !mbar_wait(&bars->q_empty, (items_done - 1) & 1, abort_flag)) goto prod_fail;
-      {
+    const int rid = resolver_id(ptid);  // >= 0 for the table resolvers
+    uint32_t g = 0, items_done = 0;
+    bool ok = true;
+    Cursor cur = first_cursor(p);
+    Cursor nxt = next_cursor(p, cur);
+    uint4 raw[kItemsPerThread];
+    int scl[kItemsPerThread];
+    // Resolve pipeline (threads < kSlots): `pend` is this thread's slot entry of
+    // block g+1 (its scale bytes were requested a step ago) and `ps` the index
+    // of block g+2 (requested a step ago); both stages hide a memory latency.
+    Cursor nxt2 = next_cursor(p, nxt);
+    SlotEntry pend;
+    pend.row = nullptr;
+    pend.scales = make_uint2(0, 0);
+    PendingSlot ps;
+    ps.loc = -1;
+    ps.main = true;
+    if (cur.valid) {
+      resolve_block(p, cur.sp, cur.item / p.groups, cur.blk, rid, tabs);
+      if (nxt.valid) pend = finish_slot(p, slot_loc(p, nxt.sp, nxt.item / p.groups, nxt.blk, rid));
+      if (nxt2.valid) ps = slot_loc(p, nxt2.sp, nxt2.item / p.groups, nxt2.blk, rid);
+      named_bar_sync(2, kProdThreads);
+      load_block_items(tabs, ptid, raw, scl);
+    }
+    while (cur.valid) {
+      const int q = cur.item / p.groups, hg = cur.item - q * p.groups;
+      const Cursor nxt3 = next_cursor(p, nxt2);
+      if (nxt.valid && rid >= 0) tabs[((g + 1) % kTabBufs) * kSlots + rid] = pend;
+      // Table of block g+1 is complete; leave together if any producer gave up.
+      if (!group_sync_and(2, kProdThreads, ok)) goto prod_fail;
+      if (nxt2.valid) pend = finish_slot(p, ps);  // block g+2; scale bytes land by the next step
+      if (nxt3.valid) ps = slot_loc(p, nxt3.sp, nxt3.item / p.groups, nxt3.blk, rid);
+      if (cur.blk == 0) {
+        if (items_done > 0) ok = ok && mbar_wait(&bars->q_empty, (items_done - 1) & 1, abort_flag);
         const QT* qsrc = static_cast<const QT*>(p.q) + size_t(q) * p.heads * kDim;
-#pragma unroll 4
-        for (int k = 0; k < 16; ++k) {
-          const int i = ptid + kProdThreads * k;
+#pragma unroll 2
+        for (int i = ptid; i < kHeads * 64; i += kProdThreads) {
           const int row = i >> 6, c = i & 63;
           const int head = hg * kHeads + row;
-          uint4 v = make_uint4(0, 0, 0, 0);
-          if (head < p.heads) v = load_q8_bf16<QT>(qsrc + size_t(head) * kDim + c * 8);
-          st_shared_v4(q_base + uint32_t(c >> 3) * (kHeads * 128) + sw128(row, c & 7), v);
-        }
-      }
-      fence_proxy_async_smem();
-      mbar_arrive(&bars->q_full);
-
-      for (int blk = 0; blk < nblk; ++blk, ++blocks_done) {
-        // Gather this block's rows into registers (the loads overlap the MMAs
-        // and softmax of the previous block).
-        uint4 raw[18];
-        int scl[18];
-        {
-          const int cA = ptid & 7;
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const int slot = (ptid >> 3) + 32 * k;
-            SlotRef r;
-            const bool ok = resolve_slot(p, sp, q, blk * kSlots + slot, r, true);
-#pragma unroll
-            for (int m = 0; m < 3; ++m) {
-              const int c = 8 * m + cA;
-              raw[m * 4 + k] = ok ? ldg_stream(r.data + c * 16) : make_uint4(0, 0, 0, 0);
-              scl[m * 4 + k] = ok ? int(__ldg(r.scale + (c >> 2))) : -1;
-            }
-          }
-#pragma unroll
-          for (int k = 0; k < 6; ++k) {
-            const int i = ptid + kProdThreads * k;
-            const int slot = i / 12, c = 24 + i % 12;
-            SlotRef r;
-            const bool ok = resolve_slot(p, sp, q, blk * kSlots + slot, r, false);
-            raw[12 + k] = ok ? ldg_stream(r.data + c * 16) : make_uint4(0, 0, 0, 0);
-            scl[12 + k] = ok ? (c < 28 ? int(__ldg(r.scale + (c >> 2))) : 0) : -1;
-          }
-        }
-        // Dequantise into the K pairs as they free up.
-#pragma unroll
-        for (int m = 0; m < 4; ++m) {
-          if (blocks_done > 0 && !mbar_wait(&bars->k_empty[m], (blocks_done - 1) & 1, abort_flag)) goto prod_fail;
-          if (m < 3) {
-            const int c = 8 * m + (ptid & 7);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const int slot = (ptid >> 3) + 32 * k;
-              if (scl[m * 4 + k] >= 0)
-                store_k_chunk(k_base, slot, c, raw[m * 4 + k], scl[m * 4 + k]);
-              else
-                zero_k_chunk(k_base, slot, c);
-            }
+          const uint32_t dst = q_base + uint32_t(c >> 3) * (kHeads * 128) + sw128(row, c & 7);
+          if (head >= p.heads) {
+            st_shared_v4(dst, make_uint4(0, 0, 0, 0));
+          } else if constexpr (std::is_same<QT, __nv_bfloat16>::value) {
+            cp_async16(dst, qsrc + size_t(head) * kDim + c * 8);
           } else {
-#pragma unroll
-            for (int k = 0; k < 6; ++k) {
-              const int i = ptid + kProdThreads * k;
-              const int slot = i / 12, c = 24 + i % 12;
-              if (scl[12 + k] >= 0)
-                store_k_chunk(k_base, slot, c, raw[12 + k], scl[12 + k]);
-              else
-                zero_k_chunk(k_base, slot, c);
-            }
+            st_shared_v4(dst, load_q8_bf16<QT>(qsrc + size_t(head) * kDim + c * 8));
           }
-          fence_proxy_async_smem();
-          mbar_arrive(&bars->k_full[m]);
         }
       }
-      ++items_done;
+      if (ptid == 0) DSV4_TRACE(items_done, cur.blk, 0);
+      const int b = g % kKBufs;
+      const uint32_t kbuf = k_base + uint32_t(b) * kBlockBytes;
+      const SlotEntry* ntab = tabs + ((g + 1) % kTabBufs) * kSlots;
+#define DSV4_STORE_PAIR(M)                                                                          \
+  do {                                                                                              \
+    if (g >= kKBufs) ok = ok && mbar_wait(&bars->k_empty[b][M], ((g / kKBufs) - 1) & 1, abort_flag); \
+    store_pair_items<M>(kbuf, ptid, raw, scl);                                                      \
+    fence_proxy_async_smem();                                                                       \
+    mbar_arrive(&bars->k_full[b][M]);                                                               \
+    if (nxt.valid) load_pair_items<M>(ntab, ptid, raw, scl);                                        \
+  } while (0)
+      DSV4_STORE_PAIR(0);
+      if (cur.blk == 0) {
+        // Q has landed by now: make it visible to the tensor cores and signal it.
+        cp_async_wait_all();
+        fence_proxy_async_smem();
+        mbar_arrive(&bars->q_full);
+      }
+      if (ptid == 0) DSV4_TRACE(items_done, cur.blk, 1);
+      DSV4_STORE_PAIR(1);
+      DSV4_STORE_PAIR(2);
+      DSV4_STORE_PAIR(3);
+#undef DSV4_STORE_PAIR
+      if (ptid == 0) DSV4_TRACE(items_done, cur.blk, 2);
+      ++g;
+      if (cur.blk == cur.nblk - 1) ++items_done;
+      cur = nxt;
+      nxt = nxt2;
+      nxt2 = nxt3;
     }
+    if (!ok) goto prod_fail;
     if (false) {
     prod_fail:
       failed = true;
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
+    // Issue order: QK(0), then per block g: QK(g+1), PV(g).  QK(g+1) runs on the
+    // tensor pipe while the softmax works on block g.
     if (lane == 0) {
-      uint32_t items_done = 0, blocks_done = 0;
-      for (int item = blockIdx.x; item < p.num_items; item += gridDim.x) {
-        const int q = item / p.groups;
-        const SlotSpace sp = slot_space(p, q);
-        const int nblk = sp.blocks();
-        if (nblk == 0) continue;
-        if (!mbar_wait(&bars->q_full, items_done & 1, abort_flag)) goto mma_fail;
-        for (int blk = 0; blk < nblk; ++blk, ++blocks_done) {
-          const uint32_t par = blocks_done & 1;
-          // S^T = K . Q^T over the 512 dims, pair by pair as the producers fill them.
-          for (int m = 0; m < 4; ++m) {
-            if (!mbar_wait(&bars->k_full[m], par, abort_flag)) goto mma_fail;
+      uint32_t gq = 0, gp = 0, q_items = 0, pv_items = 0;
+      Cursor qk = first_cursor(p);
+      Cursor pv = qk;
+      bool ok = true;
+      bool first = true;
+      while (ok && pv.valid) {
+        // QK of the next block (block 0 before the first PV).
+        for (int rep = first ? 2 : 1; rep > 0 && qk.valid && ok; --rep) {
+          if (qk.blk == 0) {
+            if (!(ok = mbar_wait(&bars->q_full, q_items & 1, abort_flag))) break;
+            ++q_items;
+          }
+          const int bq = gq % kKBufs;
+          const uint32_t kbufq = k_base + uint32_t(bq) * kBlockBytes;
+          for (int m = 0; m < 4 && ok; ++m) {
+            if (!(ok = mbar_wait(&bars->k_full[bq][m], (gq / kKBufs) & 1, abort_flag))) break;
+            if (m == 0) DSV4_TRACE(q_items - 1, qk.blk, 3);
             tc_fence_after();
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
               const int sub = 2 * m + h;
 #pragma unroll
               for (int kk = 0; kk < 4; ++kk) {
-                const uint64_t a = smem_desc_sw128(k_base + sub * kSubTileBytes + kk * 32, 16, 1024);
-                const uint64_t b = smem_desc_sw128(q_base + sub * (kHeads * 128) + kk * 32, 16, 1024);
-                mma_bf16_ss(tmem + kTmemS, a, b, kIdescQK, (sub | kk) != 0);
+                const uint64_t a = smem_desc_sw128(kbufq + sub * kSubTileBytes + kk * 32, 16, 1024);
+                const uint64_t bd = smem_desc_sw128(q_base + sub * (kHeads * 128) + kk * 32, 16, 1024);
+                mma_bf16_ss(tmem + kTmemS + 64 * bq, a, bd, kIdescQK, (sub | kk) != 0);
               }
             }
           }
-          mma_commit(&bars->s_full);
-          if (blk == nblk - 1) mma_commit(&bars->q_empty);
-          if (!mbar_wait(&bars->p_full, par, abort_flag)) goto mma_fail;
-          if (blk == 0 && items_done > 0 && !mbar_wait(&bars->o_empty, (items_done - 1) & 1, abort_flag))
-            goto mma_fail;
-          tc_fence_after();
-          // O^T[m] += V^T[m] . P^T, V^T read MN-major from the same K pair tile.
-          for (int m = 0; m < 4; ++m) {
-#pragma unroll
-            for (int kk = 0; kk < kSlots / 16; ++kk) {
-              const uint64_t a = smem_desc_sw128(k_base + m * kPairBytes + kk * 2048, kSubTileBytes, 1024);
-              const uint64_t b = smem_desc_sw128(p_base + kk * 2048, kSubTileBytes, 1024);
-              mma_bf16_ss(tmem + 64 * m, a, b, kIdescPV, (blk | kk) != 0);
-            }
-            mma_commit(&bars->k_empty[m]);
-          }
-          if (blk == nblk - 1) mma_commit(&bars->o_full);
+          if (!ok) break;
+          mma_commit(&bars->s_full[bq]);
+          if (qk.blk == qk.nblk - 1) mma_commit(&bars->q_empty);
+          DSV4_TRACE(q_items - 1, qk.blk, 4);
+          ++gq;
+          qk = next_cursor(p, qk);
         }
-        ++items_done;
+        first = false;
+        if (!ok) break;
+        const int b = gp % kKBufs;
+        if (!(ok = mbar_wait(&bars->p_full[b], (gp / kKBufs) & 1, abort_flag))) break;
+        if (pv.blk == 0 && pv_items > 0 && !(ok = mbar_wait(&bars->o_empty, (pv_items - 1) & 1, abort_flag))) break;
+        DSV4_TRACE(pv_items, pv.blk, 5);
+        tc_fence_after();
+        // O^T[m] += V^T[m] . P^T, V^T read MN-major from the same K tile.
+        const uint32_t kbuf = k_base + uint32_t(b) * kBlockBytes;
+        const uint32_t pbuf = p_base + uint32_t(b) * kPBytes;
+        for (int m = 0; m < 4; ++m) {
+#pragma unroll
+          for (int kk = 0; kk < kSlots / 16; ++kk) {
+            const uint64_t a = smem_desc_sw128(kbuf + m * kPairBytes + kk * 2048, kSubTileBytes, 1024);
+            const uint64_t bd = smem_desc_sw128(pbuf + kk * 2048, kPBytes, 1024);
+            mma_bf16_ss(tmem + 64 * m, a, bd, kIdescPV, (pv.blk | kk) != 0);
+          }
+          mma_commit(&bars->k_empty[b][m]);
+        }
+        mma_commit(&bars->pv_done);
+        DSV4_TRACE(pv_items, pv.blk, 6);
+        if (pv.blk == pv.nblk - 1) {
+          mma_commit(&bars->o_full);
+          ++pv_items;
+        }
+        ++gp;
+        pv = next_cursor(p, pv);
       }
-      if (false) {
-      mma_fail:
-        failed = true;
-      }
+      if (!ok) failed = true;
     }
     __syncwarp();
   } else {
     // ------------------------------------------------------------ softmax + epilogue
-    const int t = threadIdx.x;  // TMEM lane
+    // With M = 64 the S^T row of slot 16w + i (i < 16) sits in TMEM lane 32w + i;
+    // lanes 16..31 of each warp carry no slot and contribute neutral values.
+    // The per-head running max m_use only moves when some score of the block
+    // exceeds it by more than 2^8 (block-wide vote; the column-max reduction runs
+    // only then), and the per-head sums stay per lane in TMEM (columns kTmemL+) until
+    // the query ends.
+    const int t = threadIdx.x;
+    const bool has_slot = lane < 16;
+    const int slot = 16 * warp + lane;
     const uint32_t t_lane = tmem + (uint32_t(warp * 32) << 16);
-    float lsum = 0.f;  // running sum of head t (threads 0..63)
-    uint32_t items_done = 0, blocks_done = 0;
+    const float sl2 = p.scale_log2;
     constexpr int esz = sizeof(QT);
+    // Items without any valid slot: zeros (the sink alone gives a zero output).
     for (int item = blockIdx.x; item < p.num_items; item += gridDim.x) {
       const int q = item / p.groups, hg = item - q * p.groups;
-      const SlotSpace sp = slot_space(p, q);
-      const int nblk = sp.blocks();
+      if (slot_space(p, q).blocks() != 0) continue;
       const int hcount = min(kHeads, p.heads - hg * kHeads);
       uint8_t* out_q = static_cast<uint8_t*>(p.out) + (size_t(q) * p.heads + size_t(hg) * kHeads) * kDim * esz;
-      if (nblk == 0) {
-        const int nvec = hcount * kDim * esz / 16;
-        for (int i = t; i < nvec; i += 128) reinterpret_cast<uint4*>(out_q)[i] = make_uint4(0, 0, 0, 0);
-        continue;
-      }
-      for (int blk = 0; blk < nblk; ++blk, ++blocks_done) {
-        const bool okw = mbar_wait(&bars->s_full, blocks_done & 1, abort_flag);
-        if (!soft_sync_and(okw)) goto soft_fail;
-        tc_fence_after();
-        SlotRef r;
-        const bool valid = resolve_slot(p, sp, q, blk * kSlots + t, r, false);
-        float v[64];
-        tmem_ld32(t_lane + kTmemS, v);
-        tmem_ld32(t_lane + kTmemS + 32, v + 32);
+      const int nvec = hcount * kDim * esz / 16;
+      for (int i = t; i < nvec; i += 128) reinterpret_cast<uint4*>(out_q)[i] = make_uint4(0, 0, 0, 0);
+    }
+    // This lane's partial sums of P per head (in the m_use frame) live in TMEM
+    // columns kTmemL .. kTmemL+63 until the query ends.
+    {
+      float z[32];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) z[c] = 0.f;
+      tmem_st32(t_lane + kTmemL, z);
+      tmem_st32(t_lane + kTmemL + 32, z);
+      tmem_wait_st();
+    }
+    uint32_t g = 0, items_done = 0;
+    for (Cursor cur = first_cursor(p); cur.valid; cur = next_cursor(p, cur), ++g) {
+      const int b = g % kKBufs;
+      const bool okw = mbar_wait(&bars->s_full[b], (g / kKBufs) & 1, abort_flag);
+      if (!soft_sync_and(okw)) goto soft_fail;
+      if (t == 0) DSV4_TRACE(items_done, cur.blk, 7);
+      tc_fence_after();
+      const bool valid = has_slot && tabs[(g % kTabBufs) * kSlots + slot].row != nullptr;
+      const uint32_t s_col = kTmemS + 64 * b;
+      float v[32];
+      bool over = false;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        tmem_ld32(t_lane + s_col + 32 * hh, v);
         tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < 64; ++c) v[c] = valid ? v[c] * p.scale_log2 : -INFINITY;
-        {
-          const float2 mx = warp_colreduce64<true>(v);
-          bars->red[warp][2 * lane] = mx.x;
-          bars->red[warp][2 * lane + 1] = mx.y;
-        }
+        for (int c = 0; c < 32; ++c) over |= fmaf(v[c], sl2, -bars->m_use[32 * hh + c]) > 8.f;
+      }
+      const bool rebase = group_sync_or(1, 128, valid && over);
+      if (rebase) {
+        float w64[64];
+        tmem_ld32(t_lane + s_col, w64);
+        tmem_ld32(t_lane + s_col + 32, w64 + 32);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 64; ++c) w64[c] = valid ? w64[c] * sl2 : -INFINITY;
+        const float2 mx = warp_colreduce64<true>(w64);
+        bars->red[warp][2 * lane] = mx.x;
+        bars->red[warp][2 * lane + 1] = mx.y;
         named_bar_sync(1, 128);
         if (t < kHeads) {
           float bm = bars->red[0][t];
@@ -523,50 +813,27 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
           for (int w = 1; w < kSoftWarps; ++w) bm = fmaxf(bm, bars->red[w][t]);
           const float mo = bars->m_use[t];
           float alpha = 1.f;
-          if (mo == -INFINITY) {
+          if (bm > mo + 8.f || (mo == -INFINITY && bm != -INFINITY)) {
+            alpha = mo == -INFINITY ? 0.f : exp2f(mo - bm);
             bars->m_use[t] = bm;
-          } else if (bm > mo + 8.f) {
-            alpha = exp2f(mo - bm);
-            bars->m_use[t] = bm;
-            bars->any_rescale = 1;
           }
           bars->alpha[t] = alpha;
-          lsum *= alpha;
         }
         named_bar_sync(1, 128);
-        // P^T row t = exp2(s - m_use), written as bf16 in the swizzled MN-major layout.
-        tmem_ld32(t_lane + kTmemS, v);
-        tmem_ld32(t_lane + kTmemS + 32, v + 32);
-        tmem_wait_ld();
+#pragma unroll 1
+        for (int hh = 0; hh < 2; ++hh) {
+          tmem_ld32(t_lane + kTmemL + 32 * hh, v);
+          tmem_wait_ld();
 #pragma unroll
-        for (int cc = 0; cc < 8; ++cc) {
-          uint32_t w4[4];
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int c = cc * 8 + 2 * j;
-            const float m0 = bars->m_use[c], m1 = bars->m_use[c + 1];
-            const float p0 = (valid && m0 != -INFINITY) ? exp2f(fmaf(v[c], p.scale_log2, -m0)) : 0.f;
-            const float p1 = (valid && m1 != -INFINITY) ? exp2f(fmaf(v[c + 1], p.scale_log2, -m1)) : 0.f;
-            v[c] = p0;
-            v[c + 1] = p1;
-            const __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
-            w4[j] = *reinterpret_cast<const uint32_t*>(&b2);
-          }
-          st_shared_v4(p_base + sw128(t, cc), make_uint4(w4[0], w4[1], w4[2], w4[3]));
+          for (int c = 0; c < 32; ++c) v[c] *= bars->alpha[32 * hh + c];
+          tmem_st32(t_lane + kTmemL + 32 * hh, v);
         }
-        {
-          const float2 sm = warp_colreduce64<false>(v);
-          bars->red[warp][2 * lane] = sm.x;  // the max partials were consumed before the last barrier
-          bars->red[warp][2 * lane + 1] = sm.y;
-        }
-        const bool rescale = bars->any_rescale != 0;
-        named_bar_sync(1, 128);
-        if (t < kHeads) {
-#pragma unroll
-          for (int w = 0; w < kSoftWarps; ++w) lsum += bars->red[w][t];
-        }
-        if (rescale && blk > 0) {
-          // Re-base the O^T accumulators of the heads whose max moved (columns = heads).
+        tmem_wait_st();
+        if (cur.blk > 0) {
+          // O must hold PV of the previous block before it is re-based.
+          const bool okp = mbar_wait(&bars->pv_done, (g - 1) & 1, abort_flag);
+          if (!soft_sync_and(okp)) goto soft_fail;
+          tc_fence_after();
 #pragma unroll 1
           for (int m = 0; m < 4; ++m)
 #pragma unroll 1
@@ -579,20 +846,66 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
             }
           tmem_wait_st();
         }
-        named_bar_sync(1, 128);  // red / alpha / any_rescale consumed
-        if (t == 0) bars->any_rescale = 0;
-        fence_proxy_async_smem();
-        tc_fence_before();
-        mbar_arrive(&bars->p_full);
+        named_bar_sync(1, 128);  // alpha consumed before the next re-base writes it
       }
+      if (t == 0) DSV4_TRACE(items_done, cur.blk, 8);
+      // P^T row = 2^(s*scale - m_use) in bf16, swizzled MN-major; sums stay per lane.
+      const uint32_t pbuf = p_base + uint32_t(b) * kPBytes;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        float la[32];
+        tmem_ld32(t_lane + s_col + 32 * hh, v);
+        tmem_ld32(t_lane + kTmemL + 32 * hh, la);
+        tmem_wait_ld();
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          uint32_t w4[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int c = 8 * cc + 2 * j;
+            const float p0 = valid ? fast_exp2(fmaf(v[c], sl2, -bars->m_use[32 * hh + c])) : 0.f;
+            const float p1 = valid ? fast_exp2(fmaf(v[c + 1], sl2, -bars->m_use[32 * hh + c + 1])) : 0.f;
+            la[c] += p0;
+            la[c + 1] += p1;
+            const __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
+            w4[j] = *reinterpret_cast<const uint32_t*>(&b2);
+          }
+          if (has_slot) st_shared_v4(pbuf + sw128(slot, 4 * hh + cc), make_uint4(w4[0], w4[1], w4[2], w4[3]));
+        }
+        tmem_st32(t_lane + kTmemL + 32 * hh, la);
+      }
+      tmem_wait_st();
+      fence_proxy_async_smem();
+      tc_fence_before();
+      if (t == 0) DSV4_TRACE(items_done, cur.blk, 9);
+      mbar_arrive(&bars->p_full[b]);
+      if (cur.blk != cur.nblk - 1) continue;
+
       // -------------------------------------------------------------- epilogue
+      const int q = cur.item / p.groups, hg = cur.item - q * p.groups;
+      const int hcount = min(kHeads, p.heads - hg * kHeads);
+      uint8_t* out_q = static_cast<uint8_t*>(p.out) + (size_t(q) * p.heads + size_t(hg) * kHeads) * kDim * esz;
       {
-        const bool okw = mbar_wait(&bars->o_full, items_done & 1, abort_flag);
-        if (!soft_sync_and(okw)) goto soft_fail;
+        // Per-head sums: reduce the lanes' partials once per query.
+        float la[64];
+        tmem_ld32(t_lane + kTmemL, la);
+        tmem_ld32(t_lane + kTmemL + 32, la + 32);
+        tmem_wait_ld();
+        const float2 sm = warp_colreduce64<false>(la);
+        bars->red[warp][2 * lane] = sm.x;
+        bars->red[warp][2 * lane + 1] = sm.y;
+#pragma unroll
+        for (int c = 0; c < 32; ++c) la[c] = 0.f;
+        tmem_st32(t_lane + kTmemL, la);
+        tmem_st32(t_lane + kTmemL + 32, la);
+        tmem_wait_st();
+        const bool okw2 = mbar_wait(&bars->o_full, items_done & 1, abort_flag);
+        if (!soft_sync_and(okw2)) goto soft_fail;
       }
+      if (t == 0) DSV4_TRACE(items_done, 0, 10);
       tc_fence_after();
       if (t < kHeads) {
-        float total = lsum;
+        float total = bars->red[0][t] + bars->red[1][t] + bars->red[2][t] + bars->red[3][t];
         const float mu = bars->m_use[t];
         if (p.sink != nullptr && hg * kHeads + t < p.heads) {
           const float sk = p.sink[hg * kHeads + t] * kLog2e;
@@ -600,37 +913,34 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
         }
         bars->inv_l[t] = (total > 0.f && total != INFINITY) ? 1.f / total : 0.f;
         bars->m_use[t] = -INFINITY;
-        lsum = 0.f;
       }
       named_bar_sync(1, 128);
       {
-        constexpr int rows_per_pass = int(kPBytes / (128 * esz));  // heads staged per pass
-        constexpr int vec_per_row = 128 * esz / 16;
-        uint8_t* stage = smem + kOffP;
-        float v[64];
+        // Lane pairs (dims d, d+1) swap halves so each lane stores 2 adjacent dims
+        // of one head: a warp store covers two 64-byte runs of two head rows.
+        const bool odd = (lane & 1) != 0;
         for (int m = 0; m < 4; ++m) {
-          tmem_ld32(t_lane + 64 * m, v);
-          tmem_ld32(t_lane + 64 * m + 32, v + 32);
+          float o[64];
+          tmem_ld32(t_lane + 64 * m, o);
+          tmem_ld32(t_lane + 64 * m + 32, o + 32);
           tmem_wait_ld();
-          for (int h0 = 0; h0 < kHeads; h0 += rows_per_pass) {
+          const int d = 128 * m + t;  // this lane's dim
 #pragma unroll
-            for (int c = 0; c < 64; ++c) {
-              if (c >= h0 && c < h0 + rows_per_pass)
-                reinterpret_cast<QT*>(stage)[(c - h0) * 128 + t] = Elem<QT>::from_f(v[c] * bars->inv_l[c]);
-            }
-            named_bar_sync(1, 128);
-            const int rows = min(rows_per_pass, hcount - h0);
-            for (int i = t; i < rows * vec_per_row; i += 128) {
-              const int h = i / vec_per_row, vv = i - h * vec_per_row;
-              uint4* dst = reinterpret_cast<uint4*>(out_q + (size_t(h0 + h) * kDim + 128 * m) * esz) + vv;
-              *dst = reinterpret_cast<const uint4*>(stage)[h * vec_per_row + vv];
-            }
-            named_bar_sync(1, 128);
+          for (int j = 0; j < 32; ++j) {
+            const float a0 = o[2 * j] * bars->inv_l[2 * j];
+            const float a1 = o[2 * j + 1] * bars->inv_l[2 * j + 1];
+            const float recv = __shfl_xor_sync(0xffffffffu, odd ? a0 : a1, 1);
+            const int h = odd ? 2 * j + 1 : 2 * j;
+            const float lo = odd ? recv : a0;
+            const float hi = odd ? a1 : recv;
+            if (h < hcount) store_pair(reinterpret_cast<QT*>(out_q) + size_t(h) * kDim + (odd ? d - 1 : d), lo, hi);
           }
         }
       }
       tc_fence_before();
+      if (t == 0) DSV4_TRACE(items_done, 0, 11);
       mbar_arrive(&bars->o_empty);
+      named_bar_sync(1, 128);  // inv_l / red consumed before the next query reuses them
       ++items_done;
     }
     if (false) {
@@ -734,3 +1044,12 @@ extern "C" int csahca_dsv4_decode(const void* q, int q_dtype, int64_t num_querie
     default: return csahca_set_arg_error("unsupported q dtype");
   }
 }
+
+#ifdef CSAHCA_DSV4_TRACE
+extern "C" __attribute__((visibility("default"))) int csahca_dsv4_trace_read(long long* host, int n) {
+  if (n > 2 * 8 * 16) n = 2 * 8 * 16;
+  CSAHCA_RETURN_IF_CUDA(cudaDeviceSynchronize());
+  CSAHCA_RETURN_IF_CUDA(cudaMemcpyFromSymbol(host, csahca::g_dsv4_trace, sizeof(long long) * n));
+  return CSAHCA_OK;
+}
+#endif
