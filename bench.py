@@ -170,11 +170,11 @@ def _event():
     return torch.cuda.Event(enable_timing=True)
 
 
-def bench_csa(dev, rank: int, world: int, steps: int, warmup: int, secondary: bool) -> dict:
+def bench_csa(dev, rank: int, world: int, steps: int, warmup: int, secondary: bool, batch_size: int = 64) -> dict:
     from csahca_b200 import extension as ext
     from csahca_b200 import workloads as W
 
-    batch = W.csa_batched(dev, seed=1000 * rank)
+    batch = W.csa_batched(dev, batch=batch_size, seed=1000 * rank)
     nbytes = W.csa_algorithmic_bytes(batch)
     q, k, v, lens, c, top_k = batch.q, batch.k, batch.v, batch.seq_lens, batch.chunk, batch.top_k
     torch.cuda.synchronize(dev)
@@ -339,6 +339,7 @@ def main() -> int:
     ap.add_argument("--cpu-requests", type=int, default=8, help="requests in one CPU-oracle sample")
     ap.add_argument("--workload", choices=["csa_batched", "dsv4_c0", "dsv4_c4", "dsv4_c128"], default="csa_batched",
                     help="dsv4_*: time only that DSV4 case (profiling / diagnosis); prints kernel timings")
+    ap.add_argument("--batch", type=int, default=64, help="csa_batched: override the batch (profiling only)")
     ap.add_argument("--queries", type=int, default=0, help="dsv4_*: override the number of queries")
     ap.add_argument("--context", type=int, default=0, help="dsv4_c4/c128: override the per-request context")
     a = ap.parse_args()
@@ -381,7 +382,7 @@ def main() -> int:
         res = bench_dsv4_case(dev, _peaks()[0], kw, iters=a.steps, warm=max(3, a.warmup))
         print(json.dumps({"workload": a.workload, "config": {k: str(v) for k, v in kw.items()}, **res}), flush=True)
         return 0
-    r = bench_csa(dev, rank, world, a.steps, a.warmup, secondary=(world == 1 and not a.no_secondary))
+    r = bench_csa(dev, rank, world, a.steps, a.warmup, secondary=(world == 1 and not a.no_secondary), batch_size=a.batch)
     if rank == 0:
         ms = r["total_ms"] / a.steps
         value = world * 64 / (ms / 1e3)
@@ -390,7 +391,7 @@ def main() -> int:
                 "warmup": a.warmup, "ms_per_step": round(ms, 4), "us_per_step": round(ms * 1e3, 1),
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
                 "data": "synthetic (seeded, config-2 distributions; no dataset exists for this path)",
-                "config": dict(CONFIG, parallelism=f"request-sharded x{world}, no collective"),
+                "config": dict(CONFIG, batch=a.batch, parallelism=f"request-sharded x{world}, no collective"),
                 "gpu_launches": 2 * a.steps,
                 "kernel_ms": {"csa_select": round(r["select_ms"], 4), "csa_decode": round(r["decode_ms"], 4)},
                 "step_achieved_gbs": r["step_gbs"], "roofline": r["roofline"], "decode_kernel": r["decode_kernel"],

@@ -15,7 +15,8 @@
 // skipped (csa_attention.cu:176-179), and so is a token at or beyond seq_len
 // (:181-184); a row with no token left yields zeros (:88).
 //
-// Workspace (zero on entry, zero on exit):
+// Workspace (any content on entry; the counters are cleared by a memset on the
+// call's stream):
 //   [0, 4*BH) arrival counters (rounded up to 256 B), then fp32 partials
 //   [BH][U][D+2] = (acc[D], max, sum).
 #include <algorithm>
@@ -320,6 +321,11 @@ extern "C" int csahca_csa_decode(const void* q, const void* k_cache, const void*
   p.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + align256(size_t(rows) * 4));
   p.scale_log2 = float(1.0 / sqrt(double(head_dim))) * kLog2e;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // The arrival counters must start at zero.  Kernels reset them on exit, but
+  // the partials of an earlier call with fewer rows may lie where this call's
+  // counters are, so they are cleared here (a few KB) instead of having the
+  // combine wipe every partial it read.
+  if (p.units > 1) CSAHCA_RETURN_IF_CUDA(cudaMemsetAsync(p.counters, 0, size_t(rows) * 4, s));
   switch (dtype) {
     case CSAHCA_DTYPE_BF16: return dispatch_decode_dim<__nv_bfloat16>(head_dim, p, rows, index_dtype, s);
     case CSAHCA_DTYPE_F16: return dispatch_decode_dim<__half>(head_dim, p, rows, index_dtype, s);
@@ -390,10 +396,8 @@ extern "C" int csahca_csa_decode_noalloc(const void* q, const void* k_cache, con
   void* scratch = nullptr;
   const int st = noalloc_scratch(&scratch);
   if (st != CSAHCA_OK) return st;
-  // The counters must start at zero; clear them on the caller's stream (no allocation).
-  const int64_t rows = batch * heads;
-  if (rows > 0)
-    CSAHCA_RETURN_IF_CUDA(cudaMemsetAsync(scratch, 0, align256(size_t(rows) * 4), static_cast<cudaStream_t>(stream)));
+  // csahca_csa_decode clears the counters it uses on the caller's stream, so
+  // the scratch needs no preparation here.
   return csahca_csa_decode(q, k_cache, v_cache, chunk_indices, index_dtype, dtype, batch, heads, seq_len, head_dim,
                            top_k, chunk_size, out, scratch, kNoAllocScratchBytes, stream);
 }

@@ -92,8 +92,9 @@ int csahca_csa_select_topk(const void* q, const void* k_cache, const int32_t* se
  * and tokens at or beyond S are skipped; a (b,h) with no token left gets zeros.
  * The tile size of the reference is a tuning knob only and has no counterpart:
  * results do not depend on it.
- * workspace: csahca_csa_decode_workspace_size() bytes, same zero-fill contract
- *   as the scorer's (a separate buffer).  head_dim in {32, 64, 128, 256, 512}.
+ * workspace: csahca_csa_decode_workspace_size() bytes of any content (the call
+ *   clears the part it needs with a memset on `stream`); calls that may run
+ *   concurrently must not share it.  head_dim in {32, 64, 128, 256, 512}.
  */
 size_t csahca_csa_decode_workspace_size(int64_t batch, int64_t heads, int64_t head_dim, int64_t top_k,
                                         int64_t chunk_size);

@@ -156,6 +156,33 @@ def test_topk_larger_than_chunks_and_empty_requests(cuda):
     np.testing.assert_array_equal(sel.cpu().numpy(), csa.select_topk_chunks_ragged(qn, kn, lens, c, 4, "bf16"))
 
 
+@pytest.mark.parametrize("c,d,dtype", [(1, 128, "bf16"), (3, 64, "f16"), (48, 128, "bf16"), (32, 128, "f32"),
+                                         (128, 64, "bf16"), (128, 32, "f32")])
+def test_chunk_sizes_and_unit_sizes(cuda, c, d, dtype):
+    """Odd chunk sizes (partial token steps), chunks that exactly fill a staging
+    slot, and enough rows that the scorer uses its largest ticket units."""
+    rng = np.random.default_rng(c * 7 + d)
+    n_chunks = 160 if c <= 48 else 40
+    b, h, s, k = 5, 40, c * n_chunks, 9
+    qn = from_f32(rng.standard_normal((b, h, d)).astype(np.float32), dtype)
+    kn = from_f32(rng.standard_normal((b, h, s, d)).astype(np.float32), dtype)
+    lens = (rng.integers(0, n_chunks + 1, b) * c).astype(np.int32)
+    q, kc = (to_torch(x, dtype, cuda) for x in (qn, kn))
+    sel = _ext().select_topk_chunks(q, kc, c, k, seq_lens=torch.from_numpy(lens).to(cuda)).cpu().numpy()
+    ref = csa.select_topk_chunks_ragged(qn, kn, lens, c, k, dtype)
+    np.testing.assert_array_equal(sel < 0, ref < 0)
+    # Exact indices, except that two chunks whose oracle scores agree to fp32
+    # rounding of a differently ordered sum may trade places.
+    for bi in range(b):
+        if lens[bi] == 0:
+            continue
+        sc = csa.chunk_scores(qn[bi:bi + 1], kn[bi:bi + 1, :, : lens[bi]], c, dtype)[0]
+        got = np.take_along_axis(sc, np.maximum(sel[bi], 0), -1)
+        want = np.take_along_axis(sc, np.maximum(ref[bi], 0), -1)
+        np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-6)
+    assert (sel == ref).mean() > 0.99
+
+
 def test_many_chunks_global_topk_path(cuda):
     """More chunks than the register top-k path holds (> 4096): the global-memory scan."""
     rng = np.random.default_rng(9)
@@ -196,3 +223,31 @@ def test_capturable_in_cuda_graph(cuda):
     torch.cuda.synchronize()
     assert torch.equal(sel, ref_sel)
     assert torch.equal(out, ref_out)
+
+
+def test_workspace_left_zero_across_shapes(cuda):
+    """Every scorer call leaves its scratch all-zero, so a later call whose arrival
+    counters fall where an earlier call kept scores starts clean; the decode
+    clears its own counters, so its scratch may hold anything."""
+    from csahca_b200 import _native
+
+    ext = _ext()
+    rng = np.random.default_rng(21)
+    shapes = [(1, 2, 64 * 600, 64, 64, 9), (6, 40, 64 * 20, 128, 64, 4), (1, 1, 16 * 5000, 32, 16, 3),
+              (8, 32, 64 * 12, 128, 64, 16)]
+    for b, h, s, d, c, k in shapes:
+        qn = from_f32(rng.standard_normal((b, h, d)).astype(np.float32), "bf16")
+        kn = from_f32(rng.standard_normal((b, h, s, d)).astype(np.float32), "bf16")
+        q, kc = (to_torch(x, "bf16", cuda) for x in (qn, kn))
+        sel = ext.select_topk_chunks(q, kc, c, k)
+        np.testing.assert_array_equal(sel.cpu().numpy(), csa.select_topk_chunks(qn, kn, c, k, "bf16"))
+        for key, buf in _native.workspaces._bufs.items():
+            if key[0] == "csa_decode":
+                buf.fill_(0xA5)
+        out = ext.csa_decode_forward_tiled(q, kc, kc, sel, c)
+        _check_out(out, csa.csa_reference(qn, kn, kn, chunk_size=c, top_k=k, dtype="bf16",
+                                          selected_chunks=sel.cpu().numpy()), "bf16")
+        torch.cuda.synchronize()
+        for key, buf in _native.workspaces._bufs.items():
+            if key[0] == "csa_select":
+                assert int(torch.count_nonzero(buf)) == 0, (key, (b, h, s, d, c, k))
