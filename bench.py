@@ -44,7 +44,12 @@ CONFIG = {"workload": "csa_batched_dynamic_decode (BASELINE config 2)", "batch":
           "dtype": "bf16", "l2": "inputs (K/V 34 GB) larger than L2; no flush"}
 # DRAM bytes per launch from one ncu capture of each kernel (profiles/*.md), scaled to the
 # bench workload by units processed; None until captured.
-NCU_TRAFFIC = {"csa_select": None}
+# DRAM bytes (read + write) per algorithmic byte of the scorer, from one ncu
+# capture (profiles/csa_select_bulk_cfg2.md): config 2 shapes at batch 4 moved
+# 483.53 MB read + 9.77 MB written for 483.43 MB algorithmic.  Traffic grows in
+# proportion to the valid K rows, so the full launch's traffic is this ratio
+# times its algorithmic bytes.
+NCU_TRAFFIC = {"csa_select": (483.53 + 9.77) / 483.43}
 
 
 def _peaks() -> tuple[float, str]:
@@ -233,7 +238,8 @@ def bench_csa(dev, rank: int, world: int, steps: int, warmup: int, secondary: bo
         "roofline": {"bound": "hbm", "kernel": "csa_select (chunk scorer + top-k)",
                      "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "peak_source": f"{peak_kind} hbm_gbs",
-                     "traffic": NCU_TRAFFIC["csa_select"],
+                     "traffic": round(NCU_TRAFFIC["csa_select"] * nbytes["scorer"]),
+                     "traffic_source": "ncu dram__bytes_read+write at batch 4, scaled by valid K bytes",
                      "algorithmic_bytes": nbytes["scorer"]},
         "decode_kernel": {"achieved_gbs": round(nbytes["decode"] / (dec_ms / 1e3) / 1e9, 1),
                           "frac": round(nbytes["decode"] / (dec_ms / 1e3) / 1e9 / hbm, 4),
