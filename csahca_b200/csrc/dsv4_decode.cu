@@ -56,10 +56,14 @@ constexpr int kHeads = 64;                    // heads per CTA item (MMA N)
 
 constexpr int kSoftWarps = 4;
 constexpr int kMmaWarp = 4;
-constexpr int kProdWarp0 = 5;
-constexpr int kProdWarps = 11;
-constexpr int kProdThreads = kProdWarps * 32;
-constexpr int kThreads = (kProdWarp0 + kProdWarps) * 32;  // 512 (4 warps per sub-partition, 128 registers)
+constexpr int kProdWarp0 = 5;   // dequantising producers: 4 threads per slot row
+constexpr int kProdWarps = 8;
+constexpr int kProdThreads = kProdWarps * 32;  // 256 = kSlots x 4
+constexpr int kResWarp0 = kProdWarp0 + kProdWarps;  // slot-table resolvers: one thread per slot
+constexpr int kResWarps = 2;
+constexpr int kResThreads = kResWarps * 32;  // 64 = kSlots
+constexpr int kQWarp = kResWarp0 + kResWarps;  // Q loader
+constexpr int kThreads = (kQWarp + 1) * 32;    // 512 (4 warps per sub-partition, 128 registers)
 
 constexpr int kKBufs = 2;                             // K tiles (and S / P buffers) in flight
 constexpr uint32_t kQBytes = kHeads * kDim * 2;      // 65536
@@ -71,8 +75,9 @@ constexpr uint32_t kOffQ = 0;
 constexpr uint32_t kOffK = kOffQ + kQBytes;
 constexpr uint32_t kOffP = kOffK + kKBufs * kBlockBytes;
 constexpr uint32_t kOffBar = kOffP + kKBufs * kPBytes;
-constexpr int kTabBufs = 5;                                  // slot tables in flight (see producers)
-constexpr uint32_t kOffTab = kOffBar + 2048;
+constexpr int kTabBufs = 4;                                  // slot tables in flight (see resolvers)
+constexpr uint32_t kBarBytes = 2304;
+constexpr uint32_t kOffTab = kOffBar + kBarBytes;
 constexpr uint32_t kTabBytes = kTabBufs * kSlots * 16;      // 5 KB
 constexpr uint32_t kSmemBytes = kOffTab + kTabBytes + 1024;  // + alignment slack
 static_assert(kSmemBytes <= 232448, "shared memory budget");
@@ -89,9 +94,19 @@ __device__ long long g_dsv4_trace[2 * 8 * 16];
     if (blockIdx.x == 0 && (item_no) < 2 && (blk) < 8)                                    \
       g_dsv4_trace[((item_no) * 8 + (blk)) * 16 + (ev)] = clock64();                      \
   } while (0)
+// Per producer thread of CTA 0: cycles spent in each producer phase.
+__device__ long long g_dsv4_prod[512 * 4];
+#define DSV4_T0() long long _t0 = clock64()
+#define DSV4_ACC(k) (_acc[k] += clock64() - _t0, _t0 = clock64())
 #else
 #define DSV4_TRACE(item_no, blk, ev) \
   do {                               \
+  } while (0)
+#define DSV4_T0() \
+  do {            \
+  } while (0)
+#define DSV4_ACC(k) \
+  do {              \
   } while (0)
 #endif
 
@@ -123,6 +138,7 @@ struct Bars {
   uint64_t k_full[kKBufs][4], k_empty[kKBufs][4];
   uint64_t s_full[kKBufs], p_full[kKBufs];
   uint64_t o_full, o_empty, pv_done;
+  uint64_t tab_full[kTabBufs], tab_empty[kTabBufs];
   uint32_t tmem_base;
   int abort_flag;
   float red[kSoftWarps][kHeads];  // per-warp column partials
@@ -130,7 +146,7 @@ struct Bars {
   float alpha[kHeads];            // O/l rescale factors of the current block
   float inv_l[kHeads];            // final normalisers
 };
-static_assert(sizeof(Bars) <= 2048, "barrier area too large");
+static_assert(sizeof(Bars) <= kBarBytes, "barrier area too large");
 
 // Valid-slot space of a query: main slots then extra slots.
 struct SlotSpace {
@@ -151,18 +167,6 @@ __device__ __forceinline__ SlotSpace slot_space(const Dsv4Params& p, int q) {
   s.len_extra = lx;
   return s;
 }
-
-// Producer work items of a block: (slot, 16-byte chunk) pairs grouped by K pair
-// m (dims 128m..128m+127): pairs 0-2 hold nope chunks 8m..8m+7 (8 per slot),
-// pair 3 holds nope chunks 24-27 and the 8 rope chunks (12 per slot).
-// Thread ptid takes items ptid, ptid + kProdThreads, ... of each pair.
-__host__ __device__ constexpr int pair_chunks(int m) { return m < 3 ? 8 : 12; }
-__host__ __device__ constexpr int pair_items(int m) { return kSlots * pair_chunks(m); }
-__host__ __device__ constexpr int per_thread(int m) { return (pair_items(m) + kProdThreads - 1) / kProdThreads; }
-__host__ __device__ constexpr int item_off(int m) { return m == 0 ? 0 : item_off(m - 1) + per_thread(m - 1); }
-// Producer threads 0..kSlots-1 also resolve the slot tables (one slot each); -1 for the rest.
-__device__ __forceinline__ int resolver_id(int ptid) { return ptid < kSlots ? ptid : -1; }
-constexpr int kItemsPerThread = item_off(3) + per_thread(3);
 
 // One resolved slot of a block: its 576-byte row (nullptr = skipped) and its 8 scale bytes.
 struct SlotEntry {
@@ -271,44 +275,45 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
-// 16 e4m3 bytes x 2^(s-127) -> 16 bf16 (exact).  The e4m3 exponent/mantissa
-// bits are placed into a bf16 pattern (value x 2^-120, subnormals included) and
-// one bf16x2 multiply by 2^(s-7) restores the magnitude and applies the scale.
-__device__ __forceinline__ uint32_t e4m3x2_bits_to_bf16x2(uint32_t w, int hi) {
-  const uint32_t mag = w & 0x7F7F7F7Fu;
-  const uint32_t m = __byte_perm(mag, 0u, hi ? 0x4342u : 0x4140u) << 4;
-  const uint32_t s = __byte_perm(w, 0u, hi ? 0x3424u : 0x1404u) & 0x80008000u;
-  return m | s;
-}
-
+// 16 e4m3 bytes x 2^(s-127) -> 16 bf16 (exact).  Each e4m3 byte's magnitude
+// bits are moved to bits 4..10 of a bf16 lane and its sign to bit 15, which
+// reads as value x 2^-120 (e4m3 subnormals included); one bf16x2 multiply by
+// 2^(s-7) then restores the magnitude and applies the scale.
 __device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
   uint32_t d;
   asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
   return d;
 }
 
-__device__ __forceinline__ void dequant16(const uint4& raw, int scale_u8, uint4& lo, uint4& hi) {
+// Bytes 2k, 2k+1 of a word (magnitudes in `mag`, signs in `sgn`) -> bf16x2 bits.
+template <int K>
+__device__ __forceinline__ uint32_t e4m3_pair_bits(uint32_t mag, uint32_t sgn) {
+  const uint32_t m = __byte_perm(mag, 0u, K == 0 ? 0x4140u : 0x4342u);  // bytes to lane bits 0..7
+  const uint32_t sg = __byte_perm(sgn, 0u, K == 0 ? 0x1404u : 0x3424u);  // signs to lane bit 15
+  return (m << 4) + sg;
+}
 
+__device__ __forceinline__ void dequant16(const uint4& raw, int scale_u8, uint4& lo, uint4& hi) {
   const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
   uint32_t o[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t mag = w[i] & 0x7F7F7F7Fu, sgn = w[i] & 0x80808080u;
+    o[2 * i] = e4m3_pair_bits<0>(mag, sgn);
+    o[2 * i + 1] = e4m3_pair_bits<1>(mag, sgn);
+  }
   if (scale_u8 <= 134) {
     const uint32_t f = uint32_t(scale_u8 + 120) << 7;  // bf16 2^(s-7)
     const uint32_t f2 = f | (f << 16);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      o[2 * i] = bf16x2_mul(e4m3x2_bits_to_bf16x2(w[i], 0), f2);
-      o[2 * i + 1] = bf16x2_mul(e4m3x2_bits_to_bf16x2(w[i], 1), f2);
-    }
+    for (int i = 0; i < 8; ++i) o[i] = bf16x2_mul(o[i], f2);
   } else {
     // 2^(s-7) overflows bf16: apply 2^120 and 2^(s-127) separately.
     const uint32_t f1 = (uint32_t(247) << 7) | (uint32_t(247) << 23);
     const uint32_t e2 = uint32_t(scale_u8) << 7;
     const uint32_t f2 = e2 | (e2 << 16);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      o[2 * i] = bf16x2_mul(bf16x2_mul(e4m3x2_bits_to_bf16x2(w[i], 0), f1), f2);
-      o[2 * i + 1] = bf16x2_mul(bf16x2_mul(e4m3x2_bits_to_bf16x2(w[i], 1), f1), f2);
-    }
+    for (int i = 0; i < 8; ++i) o[i] = bf16x2_mul(bf16x2_mul(o[i], f1), f2);
   }
   lo = make_uint4(o[0], o[1], o[2], o[3]);
   hi = make_uint4(o[4], o[5], o[6], o[7]);
@@ -322,36 +327,6 @@ __device__ __forceinline__ uint32_t sw128(int row, int c16) {
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, const uint4& v) {
   asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
                : "memory");
-}
-
-// Store chunk `c` (0..35: 28 nope chunks of 16 dims, then 8 rope chunks of 8
-// dims) of slot row `slot` into the K pair tiles.
-__device__ __forceinline__ void store_k_chunk(uint32_t k_base, int slot, int c, const uint4& raw, int scale_u8) {
-  if (c < 28) {
-    const int d0 = c * 16;           // first dim
-    const int sub = d0 >> 6;         // 0..6
-    const int c16 = (d0 & 63) >> 3;  // 0,2,4,6
-    uint4 lo, hi;
-    dequant16(raw, scale_u8, lo, hi);
-    const uint32_t t = k_base + uint32_t(sub) * kSubTileBytes;
-    st_shared_v4(t + sw128(slot, c16), lo);
-    st_shared_v4(t + sw128(slot, c16 + 1), hi);
-  } else {
-    const uint32_t t = k_base + 7u * kSubTileBytes;
-    st_shared_v4(t + sw128(slot, c - 28), raw);
-  }
-}
-
-__device__ __forceinline__ void zero_k_chunk(uint32_t k_base, int slot, int c) {
-  const uint4 z = make_uint4(0, 0, 0, 0);
-  if (c < 28) {
-    const int d0 = c * 16;
-    const uint32_t t = k_base + uint32_t(d0 >> 6) * kSubTileBytes;
-    st_shared_v4(t + sw128(slot, (d0 & 63) >> 3), z);
-    st_shared_v4(t + sw128(slot, ((d0 & 63) >> 3) + 1), z);
-  } else {
-    st_shared_v4(k_base + 7u * kSubTileBytes + sw128(slot, c - 28), z);
-  }
 }
 
 // 8 q elements -> 8 bf16 packed in a uint4.
@@ -450,50 +425,6 @@ __device__ __forceinline__ void store_pair(float* dst, float a, float b) {
   *reinterpret_cast<float2*>(dst) = make_float2(a, b);
 }
 
-// Loads / stores of one K pair's items for this producer thread (M is a
-// compile-time pair index so raw[] / scl[] stay in registers).
-template <int M>
-__device__ __forceinline__ void load_pair_items(const SlotEntry* tab, int ptid, uint4* raw, int* scl) {
-#pragma unroll
-  for (int k = 0; k < per_thread(M); ++k) {
-    const int i = ptid + kProdThreads * k;
-    const int n = item_off(M) + k;
-    raw[n] = make_uint4(0, 0, 0, 0);
-    scl[n] = -1;
-    if (i < pair_items(M)) {
-      const int c = 8 * M + i % pair_chunks(M);
-      const SlotEntry e = tab[i / pair_chunks(M)];
-      if (e.row) {
-        raw[n] = ldg_stream(e.row + c * 16);
-        scl[n] = c < 28 ? scale_byte(e.scales, c >> 2) : 0;
-      }
-    }
-  }
-}
-
-__device__ __forceinline__ void load_block_items(const SlotEntry* tab, int ptid, uint4* raw, int* scl) {
-  load_pair_items<0>(tab, ptid, raw, scl);
-  load_pair_items<1>(tab, ptid, raw, scl);
-  load_pair_items<2>(tab, ptid, raw, scl);
-  load_pair_items<3>(tab, ptid, raw, scl);
-}
-
-template <int M>
-__device__ __forceinline__ void store_pair_items(uint32_t kbuf, int ptid, const uint4* raw, const int* scl) {
-#pragma unroll
-  for (int k = 0; k < per_thread(M); ++k) {
-    const int i = ptid + kProdThreads * k;
-    if (i < pair_items(M)) {
-      const int slot = i / pair_chunks(M), c = 8 * M + i % pair_chunks(M);
-      const int n = item_off(M) + k;
-      if (scl[n] >= 0)
-        store_k_chunk(kbuf, slot, c, raw[n], scl[n]);
-      else
-        zero_k_chunk(kbuf, slot, c);
-    }
-  }
-}
-
 // Position in the CTA's sequence of (item, block) work units; empty items are skipped.
 struct Cursor {
   bool valid;
@@ -551,7 +482,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
   volatile int* abort_flag = &bars->abort_flag;
 
   if (threadIdx.x == 0) {
-    mbar_init(&bars->q_full, kProdThreads);
+    mbar_init(&bars->q_full, 32);
     mbar_init(&bars->q_empty, 1);
     for (int b = 0; b < kKBufs; ++b) {
       for (int m = 0; m < 4; ++m) {
@@ -564,6 +495,10 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
     mbar_init(&bars->o_full, 1);
     mbar_init(&bars->o_empty, kSoftWarps * 32);
     mbar_init(&bars->pv_done, 1);
+    for (int t = 0; t < kTabBufs; ++t) {
+      mbar_init(&bars->tab_full[t], kResThreads);
+      mbar_init(&bars->tab_empty[t], kProdThreads + kSoftWarps * 32);
+    }
     bars->abort_flag = 0;
     fence_mbar_init();
   }
@@ -575,129 +510,227 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
   const uint32_t tmem = bars->tmem_base;
   bool failed = false;
 
-  if (warp >= kProdWarp0) {
+  if (warp >= kProdWarp0 && warp < kProdWarp0 + kProdWarps) {
     // ------------------------------------------------------------ producers
-    // Block g goes to K buffer g%2.  One register set, rotated pair by pair:
+    // Thread (slot s, quarter r) owns 16-byte chunks c = 4i + r (i = 0..8) of
+    // slot row s in every block: chunks 0..27 are e4m3 (chunk 4i + r is dims
+    // 64i + 16r .. +15, scale group i, K sub-tile i), chunks 28..35 are the
+    // bf16 rope dims (K sub-tile 7).  The shared-memory offsets are therefore
+    // fixed per thread, and four threads read 64 contiguous bytes of a row.
+    // Block g goes to K buffer g%2.  One register set rotates pair by pair:
     // right after the stores of pair m of block g, the loads of pair m of block
-    // g+1 go out into the same registers, so each row is in flight for about a
-    // block period before it is dequantised.  Slot tables are resolved two
-    // blocks ahead (index loads two steps ahead, row address and scale-byte load
-    // one step ahead, table write at the start of a step) into
-    // tabs[g % kTabBufs]; table g is read by the loads of block g (during block
-    // g-1) and by the softmax of block g, which finishes before PV(g), i.e. before
-    // the stores of block g+2 complete; it is rewritten for block g+5 in step g+3.
-    const int ptid = threadIdx.x - kProdWarp0 * 32;
-    const int rid = resolver_id(ptid);  // >= 0 for the table resolvers
-    uint32_t g = 0, items_done = 0;
+    // g+1 go out into the same registers, so every row load has a block period
+    // to land.  Invalid slots load nothing and store zeros.
+    const int pt = threadIdx.x - kProdWarp0 * 32;
+    const int s = pt >> 2, r = pt & 3;
+    const uint32_t x7 = uint32_t(s & 7), row_off = uint32_t(s) * 128u;
+    const uint32_t off_lo = row_off + ((uint32_t(2 * r) ^ x7) << 4);
+    const uint32_t off_hi = row_off + ((uint32_t(2 * r + 1) ^ x7) << 4);
+    const uint32_t off_r0 = 7u * kSubTileBytes + row_off + ((uint32_t(r) ^ x7) << 4);
+    const uint32_t off_r1 = 7u * kSubTileBytes + row_off + ((uint32_t(r + 4) ^ x7) << 4);
+    uint4 raw[9];
+    uint2 sc = make_uint2(0, 0);
     bool ok = true;
+    uint32_t g = 0;
     Cursor cur = first_cursor(p);
-    Cursor nxt = next_cursor(p, cur);
-    uint4 raw[kItemsPerThread];
-    int scl[kItemsPerThread];
-    // Resolve pipeline (threads < kSlots): `pend` is this thread's slot entry of
-    // block g+1 (its scale bytes were requested a step ago) and `ps` the index
-    // of block g+2 (requested a step ago); both stages hide a memory latency.
-    Cursor nxt2 = next_cursor(p, nxt);
-    SlotEntry pend;
-    pend.row = nullptr;
-    pend.scales = make_uint2(0, 0);
+#define DSV4_LOAD(I, C)                                                                        \
+  raw[I] = rowp != nullptr ? ldg_stream(rowp + (C) * 16) : make_uint4(0, 0, 0, 0)
+#define DSV4_LOAD_PAIR(M)                      \
+  do {                                         \
+    if ((M) < 3) {                             \
+      DSV4_LOAD(2 * (M), 8 * (M) + r);         \
+      DSV4_LOAD(2 * (M) + 1, 8 * (M) + 4 + r); \
+    } else {                                   \
+      DSV4_LOAD(6, 24 + r);                    \
+      DSV4_LOAD(7, 28 + r);                    \
+      DSV4_LOAD(8, 32 + r);                    \
+    }                                          \
+  } while (0)
+#define DSV4_STORE_NOPE(I)                                         \
+  do {                                                             \
+    uint4 lo, hi;                                                  \
+    dequant16(raw[I], scale_byte(sc, I), lo, hi);                  \
+    st_shared_v4(kbuf + (I) * kSubTileBytes + off_lo, lo);         \
+    st_shared_v4(kbuf + (I) * kSubTileBytes + off_hi, hi);         \
+  } while (0)
+    if (cur.valid) {
+      ok = mbar_wait(&bars->tab_full[0], 0, abort_flag);
+      const SlotEntry e = tabs[s];
+      mbar_arrive(&bars->tab_empty[0]);
+      const uint8_t* rowp = e.row;
+      sc = e.scales;
+      DSV4_LOAD_PAIR(0);
+      DSV4_LOAD_PAIR(1);
+      DSV4_LOAD_PAIR(2);
+      DSV4_LOAD_PAIR(3);
+    }
+    while (ok && cur.valid) {
+      const Cursor nxt = next_cursor(p, cur);
+      const uint8_t* rowp = nullptr;
+      uint2 sc_next = make_uint2(0, 0);
+      if (nxt.valid) {
+        const int tb = (g + 1) % kTabBufs;
+        ok = mbar_wait(&bars->tab_full[tb], ((g + 1) / kTabBufs) & 1, abort_flag);
+        const SlotEntry e = tabs[tb * kSlots + s];
+        mbar_arrive(&bars->tab_empty[tb]);
+        rowp = e.row;
+        sc_next = e.scales;
+      }
+      const int b = g % kKBufs;
+      const uint32_t kbuf = k_base + uint32_t(b) * kBlockBytes;
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        if (g >= kKBufs) ok = ok && mbar_wait(&bars->k_empty[b][m], ((g / kKBufs) - 1) & 1, abort_flag);
+        if (m < 3) {
+          DSV4_STORE_NOPE(2 * m);
+          DSV4_STORE_NOPE(2 * m + 1);
+        } else {
+          DSV4_STORE_NOPE(6);
+          st_shared_v4(kbuf + off_r0, raw[7]);
+          st_shared_v4(kbuf + off_r1, raw[8]);
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&bars->k_full[b][m]);
+        if (nxt.valid) DSV4_LOAD_PAIR(m);
+      }
+#undef DSV4_STORE_NOPE
+      sc = sc_next;
+      ++g;
+      cur = nxt;
+    }
+#undef DSV4_LOAD_PAIR
+#undef DSV4_LOAD
+    if (!ok) failed = true;
+  } else if (warp >= kResWarp0 && warp < kResWarp0 + kResWarps) {
+    // ------------------------------------------------------------ slot-table resolvers
+    // Thread rs resolves slot rs of every block into tabs[j % kTabBufs]: the
+    // index load runs two blocks ahead, the row address, scale-byte load and L2
+    // prefetch of the row one block ahead, and the entry is published when the
+    // table buffer is free (every producer and softmax thread has read it).
+    // The resolvers thus run up to kTabBufs blocks ahead of the producers, and
+    // the row prefetches reach L2 long before the producers' register loads.
+    const int rs = threadIdx.x - kResWarp0 * 32;
+    bool ok = true;
+    uint32_t j = 0;
+    Cursor c0 = first_cursor(p);
+    Cursor c1 = next_cursor(p, c0);
+    Cursor c2 = next_cursor(p, c1);
+    SlotEntry e0, e1;
+    e0.row = e1.row = nullptr;
+    e0.scales = e1.scales = make_uint2(0, 0);
     PendingSlot ps;
     ps.loc = -1;
     ps.main = true;
-    if (cur.valid) {
-      resolve_block(p, cur.sp, cur.item / p.groups, cur.blk, rid, tabs);
-      if (nxt.valid) pend = finish_slot(p, slot_loc(p, nxt.sp, nxt.item / p.groups, nxt.blk, rid));
-      if (nxt2.valid) ps = slot_loc(p, nxt2.sp, nxt2.item / p.groups, nxt2.blk, rid);
-      named_bar_sync(2, kProdThreads);
-      load_block_items(tabs, ptid, raw, scl);
+    if (c0.valid) e0 = finish_slot(p, slot_loc(p, c0.sp, c0.item / p.groups, c0.blk, rs));
+    if (c1.valid) e1 = finish_slot(p, slot_loc(p, c1.sp, c1.item / p.groups, c1.blk, rs));
+    if (c2.valid) ps = slot_loc(p, c2.sp, c2.item / p.groups, c2.blk, rs);
+    while (c0.valid) {
+      const int tb = j % kTabBufs;
+      if (j >= kTabBufs && !(ok = mbar_wait(&bars->tab_empty[tb], ((j / kTabBufs) - 1) & 1, abort_flag))) break;
+      tabs[tb * kSlots + rs] = e0;
+      mbar_arrive(&bars->tab_full[tb]);
+      const Cursor c3 = next_cursor(p, c2);
+      e0 = e1;
+      if (c2.valid) e1 = finish_slot(p, ps);
+      if (c3.valid) ps = slot_loc(p, c3.sp, c3.item / p.groups, c3.blk, rs);
+      c0 = c1;
+      c1 = c2;
+      c2 = c3;
+      ++j;
     }
-    while (cur.valid) {
-      const int q = cur.item / p.groups, hg = cur.item - q * p.groups;
-      const Cursor nxt3 = next_cursor(p, nxt2);
-      if (nxt.valid && rid >= 0) tabs[((g + 1) % kTabBufs) * kSlots + rid] = pend;
-      // Table of block g+1 is complete; leave together if any producer gave up.
-      if (!group_sync_and(2, kProdThreads, ok)) goto prod_fail;
-      if (nxt2.valid) pend = finish_slot(p, ps);  // block g+2; scale bytes land by the next step
-      if (nxt3.valid) ps = slot_loc(p, nxt3.sp, nxt3.item / p.groups, nxt3.blk, rid);
-      if (cur.blk == 0) {
-        if (items_done > 0) ok = ok && mbar_wait(&bars->q_empty, (items_done - 1) & 1, abort_flag);
-        const QT* qsrc = static_cast<const QT*>(p.q) + size_t(q) * p.heads * kDim;
-#pragma unroll 2
-        for (int i = ptid; i < kHeads * 64; i += kProdThreads) {
-          const int row = i >> 6, c = i & 63;
-          const int head = hg * kHeads + row;
-          const uint32_t dst = q_base + uint32_t(c >> 3) * (kHeads * 128) + sw128(row, c & 7);
-          if (head >= p.heads) {
-            st_shared_v4(dst, make_uint4(0, 0, 0, 0));
-          } else if constexpr (std::is_same<QT, __nv_bfloat16>::value) {
-            cp_async16(dst, qsrc + size_t(head) * kDim + c * 8);
-          } else {
-            st_shared_v4(dst, load_q8_bf16<QT>(qsrc + size_t(head) * kDim + c * 8));
-          }
+    if (!ok) failed = true;
+  } else if (warp == kQWarp) {
+    // ------------------------------------------------------------ Q loader
+    // Q of an item goes into the swizzled K-major Q tile once the last QK of the
+    // previous item has read it (q_empty).
+    bool ok = true;
+    uint32_t items = 0;
+    for (int it = blockIdx.x; it < p.num_items && ok; it += gridDim.x) {
+      const int q = it / p.groups, hg = it - q * p.groups;
+      if (slot_space(p, q).blocks() == 0) continue;
+      if (items > 0 && !(ok = mbar_wait(&bars->q_empty, (items - 1) & 1, abort_flag))) break;
+      const QT* qsrc = static_cast<const QT*>(p.q) + size_t(q) * p.heads * kDim;
+#pragma unroll 4
+      for (int i = lane; i < kHeads * 64; i += 32) {
+        const int row = i >> 6, c = i & 63;
+        const int head = hg * kHeads + row;
+        const uint32_t dst = q_base + uint32_t(c >> 3) * (kHeads * 128) + sw128(row, c & 7);
+        if (head >= p.heads) {
+          st_shared_v4(dst, make_uint4(0, 0, 0, 0));
+        } else if constexpr (std::is_same<QT, __nv_bfloat16>::value) {
+          cp_async16(dst, qsrc + size_t(head) * kDim + c * 8);
+        } else {
+          st_shared_v4(dst, load_q8_bf16<QT>(qsrc + size_t(head) * kDim + c * 8));
         }
       }
-      if (ptid == 0) DSV4_TRACE(items_done, cur.blk, 0);
-      const int b = g % kKBufs;
-      const uint32_t kbuf = k_base + uint32_t(b) * kBlockBytes;
-      const SlotEntry* ntab = tabs + ((g + 1) % kTabBufs) * kSlots;
-#define DSV4_STORE_PAIR(M)                                                                          \
-  do {                                                                                              \
-    if (g >= kKBufs) ok = ok && mbar_wait(&bars->k_empty[b][M], ((g / kKBufs) - 1) & 1, abort_flag); \
-    store_pair_items<M>(kbuf, ptid, raw, scl);                                                      \
-    fence_proxy_async_smem();                                                                       \
-    mbar_arrive(&bars->k_full[b][M]);                                                               \
-    if (nxt.valid) load_pair_items<M>(ntab, ptid, raw, scl);                                        \
-  } while (0)
-      DSV4_STORE_PAIR(0);
-      if (cur.blk == 0) {
-        // Q has landed by now: make it visible to the tensor cores and signal it.
-        cp_async_wait_all();
-        fence_proxy_async_smem();
-        mbar_arrive(&bars->q_full);
-      }
-      if (ptid == 0) DSV4_TRACE(items_done, cur.blk, 1);
-      DSV4_STORE_PAIR(1);
-      DSV4_STORE_PAIR(2);
-      DSV4_STORE_PAIR(3);
-#undef DSV4_STORE_PAIR
-      if (ptid == 0) DSV4_TRACE(items_done, cur.blk, 2);
-      ++g;
-      if (cur.blk == cur.nblk - 1) ++items_done;
-      cur = nxt;
-      nxt = nxt2;
-      nxt2 = nxt3;
+      cp_async_wait_all();
+      fence_proxy_async_smem();
+      mbar_arrive(&bars->q_full);
+      ++items;
     }
-    if (!ok) goto prod_fail;
-    if (false) {
-    prod_fail:
-      failed = true;
-    }
+    if (!ok) failed = true;
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
-    // Issue order: QK(0), then per block g: QK(g+1), PV(g).  QK(g+1) runs on the
-    // tensor pipe while the softmax works on block g.
+    // Event-driven issue: PV(g) goes out as soon as the softmax has published
+    // P(g); QK(g+1) goes out pair by pair as the producers finish each K pair.
+    // QK(g) may start only once PV(g-2) is issued (that PV's p_full wait proves
+    // the softmax has finished reading S buffer g%2).  PV has priority, since it
+    // frees K pairs for the producers.
     if (lane == 0) {
       uint32_t gq = 0, gp = 0, q_items = 0, pv_items = 0;
+      int mq = 0;            // next K pair of QK(gq)
+      bool q_ready = false;  // Q of the item of QK(gq) has been waited for
       Cursor qk = first_cursor(p);
       Cursor pv = qk;
       bool ok = true;
-      bool first = true;
+      long long idle_since = -1;
       while (ok && pv.valid) {
-        // QK of the next block (block 0 before the first PV).
-        for (int rep = first ? 2 : 1; rep > 0 && qk.valid && ok; --rep) {
-          if (qk.blk == 0) {
-            if (!(ok = mbar_wait(&bars->q_full, q_items & 1, abort_flag))) break;
-            ++q_items;
-          }
-          const int bq = gq % kKBufs;
-          const uint32_t kbufq = k_base + uint32_t(bq) * kBlockBytes;
-          for (int m = 0; m < 4 && ok; ++m) {
-            if (!(ok = mbar_wait(&bars->k_full[bq][m], (gq / kKBufs) & 1, abort_flag))) break;
-            if (m == 0) DSV4_TRACE(q_items - 1, qk.blk, 3);
+        bool progressed = false;
+        if (gp < gq) {
+          const int b = gp % kKBufs;
+          bool ready = mbar_try_wait(&bars->p_full[b], (gp / kKBufs) & 1);
+          if (ready && pv.blk == 0 && pv_items > 0) ready = mbar_try_wait(&bars->o_empty, (pv_items - 1) & 1);
+          if (ready) {
+            DSV4_TRACE(pv_items, pv.blk, 5);
             tc_fence_after();
+            // O^T[m] += V^T[m] . P^T, V^T read MN-major from the same K tile.
+            const uint32_t kbuf = k_base + uint32_t(b) * kBlockBytes;
+            const uint32_t pbuf = p_base + uint32_t(b) * kPBytes;
+            for (int m = 0; m < 4; ++m) {
+#pragma unroll
+              for (int kk = 0; kk < kSlots / 16; ++kk) {
+                const uint64_t a = smem_desc_sw128(kbuf + m * kPairBytes + kk * 2048, kSubTileBytes, 1024);
+                const uint64_t bd = smem_desc_sw128(pbuf + kk * 2048, kPBytes, 1024);
+                mma_bf16_ss(tmem + 64 * m, a, bd, kIdescPV, (pv.blk | kk) != 0);
+              }
+              mma_commit(&bars->k_empty[b][m]);
+            }
+            mma_commit(&bars->pv_done);
+            DSV4_TRACE(pv_items, pv.blk, 6);
+            if (pv.blk == pv.nblk - 1) {
+              mma_commit(&bars->o_full);
+              ++pv_items;
+            }
+            ++gp;
+            pv = next_cursor(p, pv);
+            progressed = true;
+          }
+        }
+        if (!progressed && qk.valid && gq <= gp + 1) {
+          const int bq = gq % kKBufs;
+          bool ready = true;
+          if (qk.blk == 0 && !q_ready) {
+            ready = q_ready = mbar_try_wait(&bars->q_full, q_items & 1);
+            if (q_ready) ++q_items;
+          }
+          if (ready) ready = mbar_try_wait(&bars->k_full[bq][mq], (gq / kKBufs) & 1);
+          if (ready) {
+            if (mq == 0) DSV4_TRACE(q_items - 1, qk.blk, 3);
+            tc_fence_after();
+            const uint32_t kbufq = k_base + uint32_t(bq) * kBlockBytes;
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-              const int sub = 2 * m + h;
+              const int sub = 2 * mq + h;
 #pragma unroll
               for (int kk = 0; kk < 4; ++kk) {
                 const uint64_t a = smem_desc_sw128(kbufq + sub * kSubTileBytes + kk * 32, 16, 1024);
@@ -705,41 +738,31 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
                 mma_bf16_ss(tmem + kTmemS + 64 * bq, a, bd, kIdescQK, (sub | kk) != 0);
               }
             }
+            if (++mq == 4) {
+              mma_commit(&bars->s_full[bq]);
+              if (qk.blk == qk.nblk - 1) mma_commit(&bars->q_empty);
+              DSV4_TRACE(q_items - 1, qk.blk, 4);
+              mq = 0;
+              q_ready = false;
+              ++gq;
+              qk = next_cursor(p, qk);
+            }
+            progressed = true;
           }
-          if (!ok) break;
-          mma_commit(&bars->s_full[bq]);
-          if (qk.blk == qk.nblk - 1) mma_commit(&bars->q_empty);
-          DSV4_TRACE(q_items - 1, qk.blk, 4);
-          ++gq;
-          qk = next_cursor(p, qk);
         }
-        first = false;
-        if (!ok) break;
-        const int b = gp % kKBufs;
-        if (!(ok = mbar_wait(&bars->p_full[b], (gp / kKBufs) & 1, abort_flag))) break;
-        if (pv.blk == 0 && pv_items > 0 && !(ok = mbar_wait(&bars->o_empty, (pv_items - 1) & 1, abort_flag))) break;
-        DSV4_TRACE(pv_items, pv.blk, 5);
-        tc_fence_after();
-        // O^T[m] += V^T[m] . P^T, V^T read MN-major from the same K tile.
-        const uint32_t kbuf = k_base + uint32_t(b) * kBlockBytes;
-        const uint32_t pbuf = p_base + uint32_t(b) * kPBytes;
-        for (int m = 0; m < 4; ++m) {
-#pragma unroll
-          for (int kk = 0; kk < kSlots / 16; ++kk) {
-            const uint64_t a = smem_desc_sw128(kbuf + m * kPairBytes + kk * 2048, kSubTileBytes, 1024);
-            const uint64_t bd = smem_desc_sw128(pbuf + kk * 2048, kPBytes, 1024);
-            mma_bf16_ss(tmem + 64 * m, a, bd, kIdescPV, (pv.blk | kk) != 0);
-          }
-          mma_commit(&bars->k_empty[b][m]);
+        if (progressed) {
+          idle_since = -1;
+        } else {
+          // Nothing ready: sleep briefly on the barrier that is due next.
+          if (gp < gq)
+            mbar_try_wait_sleep(&bars->p_full[gp % kKBufs], (gp / kKBufs) & 1, 200u);
+          else if (qk.valid)
+            mbar_try_wait_sleep(&bars->k_full[gq % kKBufs][mq], (gq / kKBufs) & 1, 200u);
+          if (idle_since < 0)
+            idle_since = clock64();
+          else if (*abort_flag || clock64() - idle_since > 4000000000ll)
+            ok = false;
         }
-        mma_commit(&bars->pv_done);
-        DSV4_TRACE(pv_items, pv.blk, 6);
-        if (pv.blk == pv.nblk - 1) {
-          mma_commit(&bars->o_full);
-          ++pv_items;
-        }
-        ++gp;
-        pv = next_cursor(p, pv);
       }
       if (!ok) failed = true;
     }
@@ -785,6 +808,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
       if (t == 0) DSV4_TRACE(items_done, cur.blk, 7);
       tc_fence_after();
       const bool valid = has_slot && tabs[(g % kTabBufs) * kSlots + slot].row != nullptr;
+      mbar_arrive(&bars->tab_empty[g % kTabBufs]);
       const uint32_t s_col = kTmemS + 64 * b;
       float v[32];
       bool over = false;
@@ -1050,6 +1074,11 @@ extern "C" __attribute__((visibility("default"))) int csahca_dsv4_trace_read(lon
   if (n > 2 * 8 * 16) n = 2 * 8 * 16;
   CSAHCA_RETURN_IF_CUDA(cudaDeviceSynchronize());
   CSAHCA_RETURN_IF_CUDA(cudaMemcpyFromSymbol(host, csahca::g_dsv4_trace, sizeof(long long) * n));
+  return CSAHCA_OK;
+}
+extern "C" __attribute__((visibility("default"))) int csahca_dsv4_prod_read(long long* host) {
+  CSAHCA_RETURN_IF_CUDA(cudaDeviceSynchronize());
+  CSAHCA_RETURN_IF_CUDA(cudaMemcpyFromSymbol(host, csahca::g_dsv4_prod, sizeof(long long) * 512 * 4));
   return CSAHCA_OK;
 }
 #endif

@@ -40,18 +40,30 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Waits for the phase with the given parity to complete.  try_wait itself
-// blocks for a hardware-chosen interval; the clock and the abort flag are
-// checked every 64 attempts.  Gives up after ~`limit_cycles` SM clocks or once
-// *abort is set; returns false then.
+// try_wait that may suspend the thread for up to `ns` nanoseconds while the
+// phase is incomplete; the thread resumes as soon as the phase completes.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Waits for the phase with the given parity to complete.  Between checks the
+// thread sleeps inside try_wait (up to 1 us), so waiting warps take almost no
+// issue slots from the working ones.  Gives up after ~`limit_cycles` SM clocks
+// or once *abort is set; returns false then.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
                                           long long limit_cycles = 4000000000ll) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   for (;;) {
-#pragma unroll 1
-    for (int i = 0; i < 64; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, 1000u)) return true;
     if (*abort) return false;
     if (clock64() - t0 > limit_cycles) return false;
   }
