@@ -4,28 +4,31 @@
 // dsv4_decode_tile_kernel :144-271, dsv4_decode_merge_kernel :273-335).
 //
 // Per query all H heads share one 512-dim latent per slot, with V = K, so the
-// decode is two dense contractions per block of 128 slots:
-//   S^T[slot, head] = K[slot, :] . Q[head, :]          (M=128 slots, N=64 heads, K=512 dims)
-//   O^T[dim,  head] += V^T[dim, slot] . P^T[slot, head]  (M=128 dims x 4, N=64, K=128 slots)
+// decode is two dense contractions per block of 64 slots:
+//   S^T[slot, head] = K[slot, :] . Q[head, :]          (M=64 slots, N=64 heads, K=512 dims)
+//   O^T[dim,  head] += V^T[dim, slot] . P^T[slot, head]  (M=128 dims x 4, N=64, K=64 slots)
 // Both run as tcgen05.mma kind::f16 (bf16 operands, fp32 accumulators in TMEM).
 // The dequantised K tile in shared memory is written once in the 128-byte
 // swizzled layout and read as a K-major A operand by the first MMA and as an
 // MN-major A operand (V^T) by the second, so V needs no second copy.
 //
-// Warp roles (416 threads, one CTA per SM, persistent over (query, head group)):
-//   warps 0-3   softmax + epilogue; thread t owns TMEM lane t (= slot row t of
-//               S^T, = dim row t of each O^T block)
-//   warp 4      TMEM allocator + single-thread MMA issuer
-//   warps 5-12  producers: gather the block's cache rows (576 data bytes + scale
-//               bytes) straight into registers, dequantise e4m3 x 2^(s-127) to
-//               bf16 exactly, and store them into the swizzled K tile; also load Q
+// Warp roles (512 threads, one CTA per SM, persistent over (query, head group)):
+//   warps 0-3   softmax + epilogue (TMEM lanes 32w..32w+31)
+//   warp 4      TMEM allocator + single-thread, event-driven MMA issuer
+//   warps 5-12  producers: 4 threads per slot row load its 576 data bytes into
+//               registers a block ahead, dequantise e4m3 x 2^(s-127) to bf16
+//               exactly and store them into the swizzled K tile
+//   warps 13-14 slot-table resolvers (index -> row address, scale bytes, L2
+//               prefetch), up to kTabBufs blocks ahead
+//   warp 15     Q loader
 //
 // Shared memory (1024-byte aligned):
 //   Q      64 heads x 512 dims bf16, 8 K-major sub-tiles of [64 rows x 128 B]     64 KB
-//   Kpair  4 x [2 sub-tiles of 128 slot rows x 128 B] (dims 128m .. 128m+127)  128 KB
-//   P      128 slot rows x 64 heads bf16 (MN-major B of the PV MMA); also the
-//          epilogue staging buffer                                               16 KB
-// TMEM (512 columns): O^T blocks at columns 0/64/128/192, S^T at column 256.
+//   K      2 buffers x 8 sub-tiles of [64 slot rows x 128 B]                     128 KB
+//   P      2 buffers x 64 slot rows x 64 heads bf16 (MN-major B of the PV MMA)    16 KB
+//   barriers, softmax scratch, slot tables                                       ~6 KB
+// TMEM (512 columns): O^T blocks at columns 0/64/128/192, S^T buffers at 256/320,
+// per-lane P sums at 384.
 //
 // Slot semantics follow the reference: main slots [0, clamp(topk_lengths[q]))
 // then extra slots [0, clamp(extra_topk_lengths[q])) (dsv4_attention.cu:185-225);
@@ -564,7 +567,13 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
       DSV4_LOAD_PAIR(2);
       DSV4_LOAD_PAIR(3);
     }
+#ifdef CSAHCA_DSV4_TRACE
+    uint32_t p_items = 0;
+#endif
     while (ok && cur.valid) {
+#ifdef CSAHCA_DSV4_TRACE
+      if (pt == 0 && p_items == 0 && cur.blk < 8) DSV4_TRACE(0, cur.blk, 0);
+#endif
       const Cursor nxt = next_cursor(p, cur);
       const uint8_t* rowp = nullptr;
       uint2 sc_next = make_uint2(0, 0);
@@ -581,6 +590,9 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
 #pragma unroll
       for (int m = 0; m < 4; ++m) {
         if (g >= kKBufs) ok = ok && mbar_wait(&bars->k_empty[b][m], ((g / kKBufs) - 1) & 1, abort_flag);
+#ifdef CSAHCA_DSV4_TRACE
+        if (pt == 0 && m == 0 && p_items == 0 && cur.blk < 8) DSV4_TRACE(0, cur.blk, 12);
+#endif
         if (m < 3) {
           DSV4_STORE_NOPE(2 * m);
           DSV4_STORE_NOPE(2 * m + 1);
@@ -594,6 +606,10 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
         if (nxt.valid) DSV4_LOAD_PAIR(m);
       }
 #undef DSV4_STORE_NOPE
+#ifdef CSAHCA_DSV4_TRACE
+      if (pt == 0 && p_items == 0 && cur.blk < 8) DSV4_TRACE(0, cur.blk, 2);
+      if (cur.blk == cur.nblk - 1) ++p_items;
+#endif
       sc = sc_next;
       ++g;
       cur = nxt;
@@ -726,6 +742,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
           if (ready) ready = mbar_try_wait(&bars->k_full[bq][mq], (gq / kKBufs) & 1);
           if (ready) {
             if (mq == 0) DSV4_TRACE(q_items - 1, qk.blk, 3);
+            if (mq == 3) DSV4_TRACE(q_items - 1, qk.blk, 14);
             tc_fence_after();
             const uint32_t kbufq = k_base + uint32_t(bq) * kBlockBytes;
 #pragma unroll
