@@ -266,6 +266,59 @@ def _time_kernel(fn, dev, iters=50, warm=5) -> float:
     return a.elapsed_time(b) / iters
 
 
+_FLUSH: dict = {}
+
+
+def _time_flushed(fn, dev, iters=50, warm=5) -> float:
+    """Mean device time of ``fn`` with L2 flushed before every timed call (a
+    256 MB write between iterations; only ``fn`` lies inside the events)."""
+    buf = _FLUSH.get(dev)
+    if buf is None:
+        buf = _FLUSH[dev] = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for _ in range(warm):
+        fn()
+    evs = []
+    for _ in range(iters):
+        buf.fill_(1)
+        a, b = _event(), _event()
+        a.record()
+        fn()
+        b.record()
+        evs.append((a, b))
+    torch.cuda.synchronize(dev)
+    return sum(a.elapsed_time(b) for a, b in evs) / iters
+
+
+def bench_mini_block(dev) -> dict:
+    """Config 3: mini decode block (d_model 1024 = 8 x 128, seq 32768, c64 k8,
+    MLP ratio 2.0, bf16, batch 1), ms per token, L2 flushed before each step."""
+    from csahca_b200 import extension as ext
+    from csahca_b200.model_inference import DecodeStepGraph, MiniCSADecodeBlock
+
+    torch.manual_seed(0)
+    res = {}
+    g = torch.Generator(device=dev).manual_seed(0)
+    hidden = torch.randn(1, 1024, generator=g, device=dev).to(torch.bfloat16)
+    k = torch.randn(1, 8, 32768, 128, generator=g, device=dev, dtype=torch.bfloat16)
+    v = torch.randn(1, 8, 32768, 128, generator=g, device=dev, dtype=torch.bfloat16)
+    kw = dict(backend="cuda-csa-tiled", chunk_size=64, top_k=8)
+    for variant in ("reference", "rmsnorm_silu"):
+        blk = MiniCSADecodeBlock(heads=8, head_dim=128, dtype=torch.bfloat16, device=dev, mlp_ratio=2.0,
+                                 variant=variant).eval()
+        if variant == "rmsnorm_silu":
+            for lin in (blk.q_proj, blk.out_proj, blk.up_proj, blk.down_proj):
+                torch.nn.init.normal_(lin.weight, std=0.02)
+        with torch.no_grad():
+            sel = ext.select_topk_chunks(blk.q_proj(hidden).view(1, 8, 128), k, 64, 8)
+            for mode, chunks in (("precomputed", sel), ("dynamic", None)):
+                eager = _time_flushed(lambda: blk(hidden, k, v, chunks, **kw), dev, iters=100)
+                graph = DecodeStepGraph(blk, hidden, k, v, chunks, **kw)
+                graphed = _time_flushed(lambda: graph.step(hidden), dev, iters=100)
+                res[f"{variant}/{mode}"] = {"ms_per_token_eager": round(eager, 4),
+                                            "ms_per_token_graph": round(graphed, 4)}
+    return res
+
+
 DSV4_CASES = {
     "dsv4_c0 (config 4: Q128 H64 window 128, ctx 2048-16384)":
         dict(num_queries=128, heads=64, context=(2048, 16384), ratio=0, window=128),
@@ -288,7 +341,7 @@ def bench_dsv4_case(dev, hbm: float, kw: dict, iters: int = 50, warm: int = 5) -
     else:
         fn = lambda: ext.dsv4_swa_decode_forward(  # noqa: E731
             b.q, b.cache, b.token_indices, b.topk_lengths, b.attn_sink, b.page_size, b.softmax_scale)
-    ms = _time_kernel(fn, dev, iters=iters, warm=warm)
+    ms = _time_flushed(fn, dev, iters=iters, warm=warm)
     nb = W.dsv4_algorithmic_bytes(b)
     slots = b.token_indices.shape[1] + (0 if b.extra_token_indices is None else b.extra_token_indices.shape[1])
     flops = 4 * b.q.shape[0] * b.q.shape[1] * slots * 512
@@ -312,12 +365,13 @@ def bench_secondary(dev, hbm: float) -> dict:
     q = torch.randn(1, 8, 128, generator=g, device=dev, dtype=torch.bfloat16)
     k = torch.randn(1, 8, 32768, 128, generator=g, device=dev, dtype=torch.bfloat16)
     v = torch.randn(1, 8, 32768, 128, generator=g, device=dev, dtype=torch.bfloat16)
-    ms = _time_kernel(lambda: ext.csa_decode_step(q, k, v, 64, 8), dev, iters=200)
+    ms = _time_flushed(lambda: ext.csa_decode_step(q, k, v, 64, 8), dev, iters=200)
     sel = ext.select_topk_chunks(q, k, 64, 8)
-    ms_dec = _time_kernel(lambda: ext.csa_decode_forward_tiled(q, k, v, sel, 64, 8), dev, iters=200)
-    out["csa_cfg1 (config 1: B1 H8 S32768 k8)"] = {
+    ms_dec = _time_flushed(lambda: ext.csa_decode_forward_tiled(q, k, v, sel, 64, 8), dev, iters=200)
+    out["csa_cfg1 (config 1: B1 H8 S32768 k8, L2 flushed per step)"] = {
         "us_per_step_dynamic": round(ms * 1e3, 2), "us_decode_precomputed": round(ms_dec * 1e3, 2),
         "decode_gbs_selected_kv": round(8 * 512 * 128 * 2 * 2 / (ms_dec / 1e3) / 1e9, 1)}
+    out["mini_block (config 3: d1024 H8 S32768 c64 k8 mlp 2.0, ms/token, L2 flushed)"] = bench_mini_block(dev)
     return out
 
 

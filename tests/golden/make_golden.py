@@ -92,6 +92,33 @@ def dsv4_case(name, *, num_queries, heads, num_tokens, top_k, page_size, ratio, 
     print("wrote", name)
 
 
+def mini_block_case(name, *, heads, head_dim, seq_len, chunk, top_k, mlp_ratio, seed, steps):
+    """``steps`` dynamic-selection decode steps of the reference block
+    (model_inference.py MiniCSADecodeBlock, backend "torch-csa") on CPU in bf16."""
+    from hybrid_attention.model_inference import MiniCSADecodeBlock
+
+    torch.manual_seed(seed)
+    blk = MiniCSADecodeBlock(heads=heads, head_dim=head_dim, dtype=torch.bfloat16, device=torch.device("cpu"),
+                             mlp_ratio=mlp_ratio).eval()
+    g = torch.Generator().manual_seed(seed + 1)
+    hd = heads * head_dim
+    hidden = torch.randn(1, hd, generator=g).to(torch.bfloat16)
+    k = torch.randn(1, heads, seq_len, head_dim, generator=g).to(torch.bfloat16)
+    v = torch.randn(1, heads, seq_len, head_dim, generator=g).to(torch.bfloat16)
+    outs = []
+    h = hidden
+    with torch.no_grad():
+        for _ in range(steps):
+            h = blk(h, k, v, None, backend="torch-csa", chunk_size=chunk, top_k=top_k, tile_size=8)
+            outs.append(store(h))
+    arrs = dict(hidden=store(hidden), k=store(k), v=store(v), w_q=store(blk.q_proj.weight),
+                w_o=store(blk.out_proj.weight), w_up=store(blk.up_proj.weight), w_down=store(blk.down_proj.weight),
+                outs=np.stack(outs), meta=np.array([heads, head_dim, seq_len, chunk, top_k, steps]),
+                mlp_ratio=np.float64(mlp_ratio))
+    np.savez_compressed(HERE / f"{name}.npz", **arrs)
+    print("wrote", name)
+
+
 def main() -> None:
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     csa_case("csa_bf16_small", batch=1, heads=2, seq_len=512, head_dim=128, chunk=64, top_k=4, dtype="bf16", seed=0)
@@ -108,6 +135,8 @@ def main() -> None:
               extra_tokens=64, extra_top_k=8, seed=2)
     dsv4_case("dsv4_c0_f32q", num_queries=2, heads=8, num_tokens=128, top_k=16, page_size=64, ratio=0,
               extra_tokens=0, extra_top_k=0, seed=3, dtype="f32")
+    mini_block_case("mini_block", heads=2, head_dim=64, seq_len=1024, chunk=64, top_k=4, mlp_ratio=2.0, seed=0,
+                    steps=3)
 
 
 if __name__ == "__main__":
