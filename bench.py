@@ -279,6 +279,9 @@ def _time_flushed(fn, dev, iters=50, warm=5) -> float:
         fn()
     evs = []
     for _ in range(iters):
+        # Keep the GPU busy while the host enqueues the next call, so host-side
+        # launch overhead of short calls does not leak into the events.
+        torch.cuda._sleep(100_000)
         buf.fill_(1)
         a, b = _event(), _event()
         a.record()

@@ -7,20 +7,25 @@
 // stream the unit's K and V rows with 16-byte non-allocating loads (a warp step
 // covers 512 contiguous bytes: two 128-dim bf16 rows), keep an online softmax
 // per token lane group in registers, and merge warp states through shared
-// memory.  With more than one unit per row, each CTA stores its (max, sum, acc)
-// partial and the last CTA of the row (atomic arrival counter) combines them
-// and writes the output, so a decode is one launch.
+// memory.  With 2..8 units per row and a small grid (at most kClusterGridMax
+// CTAs), the row's CTAs form a thread-block cluster:
+// each leaves its (max, sum, acc) partial in shared memory and rank 0 combines
+// them through distributed shared memory.  With more units, each CTA stores its
+// partial in the workspace and the last CTA of the row (atomic arrival
+// counter) combines them.  Either way a decode is one launch.
 //
 // Token validity follows the reference: a slot with a negative chunk index is
 // skipped (csa_attention.cu:176-179), and so is a token at or beyond seq_len
 // (:181-184); a row with no token left yields zeros (:88).
 //
-// Workspace (any content on entry; the counters are cleared by a memset on the
-// call's stream):
+// Workspace (used only on the counter path; any content on entry,
+// the counters are cleared by a memset on the call's stream):
 //   [0, 4*BH) arrival counters (rounded up to 256 B), then fp32 partials
 //   [BH][U][D+2] = (acc[D], max, sum).
 #include <algorithm>
 #include <mutex>
+
+#include <cooperative_groups.h>
 
 #include "common.cuh"
 
@@ -52,7 +57,12 @@ struct DecodeParams {
   float scale_log2;  // softmax scale * log2(e)
 };
 
-template <typename T, int D, typename IdxT>
+constexpr int kMaxClusterUnits = 8;  // portable cluster size
+constexpr int64_t kClusterGridMax = 2048;
+
+// kCluster: the row's `units` CTAs form one thread-block cluster and combine
+// their partials through distributed shared memory (no workspace, no counters).
+template <typename T, int D, typename IdxT, bool kCluster>
 __global__ void __launch_bounds__(kDecThreads) csa_decode_kernel(DecodeParams p) {
   using G = RowGeom<T, D>;
   constexpr int kU = G::kVPL >= 4 ? 1 : 4 / G::kVPL;  // steps per batch (K+V loads in flight: 2*kU*kVPL)
@@ -202,6 +212,45 @@ __global__ void __launch_bounds__(kDecThreads) csa_decode_kernel(DecodeParams p)
     return;
   }
 
+  if constexpr (kCluster) {
+    namespace cg = cooperative_groups;
+    __shared__ float s_part[D];
+    __shared__ float s_ml[2];
+    for (int d = tid; d < D; d += kDecThreads) {
+      float a = 0.f;
+#pragma unroll
+      for (int w = 0; w < kDecWarps; ++w) a = fmaf(s_acc[w][d], wgt[w], a);
+      s_part[d] = a;
+    }
+    if (tid == 0) {
+      s_ml[0] = mm;
+      s_ml[1] = ll;
+    }
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();  // every CTA's partial is in its shared memory
+    if (cluster.block_rank() == 0) {
+      const int n = int(cluster.num_blocks());
+      float gm = -INFINITY;
+      for (int r = 0; r < n; ++r) gm = fmaxf(gm, cluster.map_shared_rank(s_ml, r)[0]);
+      float gl = 0.f;
+      for (int r = 0; r < n; ++r) {
+        const float* ml = cluster.map_shared_rank(s_ml, r);
+        if (ml[0] != -INFINITY) gl += ml[1] * exp2f(ml[0] - gm);
+      }
+      const float inv = gl > 0.f ? 1.f / gl : 0.f;
+      for (int d = tid; d < D; d += kDecThreads) {
+        float a = 0.f;
+        for (int r = 0; r < n; ++r) {
+          const float mu = cluster.map_shared_rank(s_ml, r)[0];
+          if (mu != -INFINITY) a = fmaf(cluster.map_shared_rank(s_part, r)[d], exp2f(mu - gm), a);
+        }
+        out[d] = Elem<T>::from_f(a * inv);
+      }
+    }
+    cluster.sync();  // peers keep their shared memory until rank 0 has read it
+    return;
+  }
+
   float* part = p.partial + (size_t(row) * p.units + unit) * (D + 2);
   for (int d = tid; d < D; d += kDecThreads) {
     float a = 0.f;
@@ -244,15 +293,36 @@ __global__ void __launch_bounds__(kDecThreads) csa_decode_kernel(DecodeParams p)
   }
 }
 
-template <typename T, int D>
-int launch_decode(const DecodeParams& p, int64_t rows, int index_dtype, cudaStream_t s) {
+template <typename T, int D, typename IdxT>
+int launch_decode_idx(const DecodeParams& p, int64_t rows, cudaStream_t s) {
   const dim3 grid(unsigned(rows * p.units));
-  if (index_dtype == CSAHCA_INDEX_I32)
-    csa_decode_kernel<T, D, int32_t><<<grid, kDecThreads, 0, s>>>(p);
-  else
-    csa_decode_kernel<T, D, int64_t><<<grid, kDecThreads, 0, s>>>(p);
+  // Small grids (latency-bound decodes) combine inside a cluster; large grids
+  // keep unconstrained CTA placement and combine through the workspace.
+  if (p.units > 1 && p.units <= kMaxClusterUnits && rows * p.units <= kClusterGridMax) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kDecThreads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = unsigned(p.units);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    CSAHCA_RETURN_IF_CUDA(cudaLaunchKernelEx(&cfg, csa_decode_kernel<T, D, IdxT, true>, p));
+  } else {
+    csa_decode_kernel<T, D, IdxT, false><<<grid, kDecThreads, 0, s>>>(p);
+  }
   CSAHCA_RETURN_IF_CUDA(cudaGetLastError());
   return CSAHCA_OK;
+}
+
+template <typename T, int D>
+int launch_decode(const DecodeParams& p, int64_t rows, int index_dtype, cudaStream_t s) {
+  if (index_dtype == CSAHCA_INDEX_I32) return launch_decode_idx<T, D, int32_t>(p, rows, s);
+  return launch_decode_idx<T, D, int64_t>(p, rows, s);
 }
 
 template <typename T>
@@ -325,7 +395,8 @@ extern "C" int csahca_csa_decode(const void* q, const void* k_cache, const void*
   // the partials of an earlier call with fewer rows may lie where this call's
   // counters are, so they are cleared here (a few KB) instead of having the
   // combine wipe every partial it read.
-  if (p.units > 1) CSAHCA_RETURN_IF_CUDA(cudaMemsetAsync(p.counters, 0, size_t(rows) * 4, s));
+  if (p.units > 1 && !(p.units <= kMaxClusterUnits && rows * p.units <= kClusterGridMax))
+    CSAHCA_RETURN_IF_CUDA(cudaMemsetAsync(p.counters, 0, size_t(rows) * 4, s));
   switch (dtype) {
     case CSAHCA_DTYPE_BF16: return dispatch_decode_dim<__nv_bfloat16>(head_dim, p, rows, index_dtype, s);
     case CSAHCA_DTYPE_F16: return dispatch_decode_dim<__half>(head_dim, p, rows, index_dtype, s);

@@ -239,10 +239,20 @@ struct StageMeta {
   int row;         // b*H + h, or -1 for the stop marker
   int chunk;
   int row_chunks;  // chunks of this row that will be scored
-  int pad;
+  int unit;        // unit-counter slot | (chunks in the unit << 8)
 };
 
-constexpr uint32_t kBulkSmem = kStages * kStageBytes + 2 * kStages * 8 + kStages * sizeof(StageMeta) + 64 + 128;
+// Per-unit arrival counters in shared memory: the warp that scores a unit's
+// last chunk publishes the whole unit to the row's global counter, so a row
+// costs one global atomic (and one fence) per unit rather than per chunk.  A
+// unit's slot is reused kUnitSlots units later; at most 2 x kStages chunks
+// (issued but not yet counted) separate the producer from the consumers, so
+// that unit has been fully counted by then.
+constexpr int kUnitSlots = 32;
+static_assert(kUnitSlots > 2 * kStages, "unit slots must outlast the chunks in flight");
+
+constexpr uint32_t kBulkSmem =
+    kStages * kStageBytes + 2 * kStages * 8 + kStages * sizeof(StageMeta) + 64 + kUnitSlots * 4 + 128;
 
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(
@@ -301,6 +311,15 @@ __device__ void warp_topk(float* scores, int n, int kout, int32_t* out) {
   for (int i = lane; i < n; i += 32) scores[i] = 0.f;
 }
 
+__device__ __forceinline__ unsigned atom_add_acq_rel_cta(unsigned* addr, unsigned v) {
+  unsigned old;
+  asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], %2;"
+               : "=r"(old)
+               : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(addr))), "r"(v)
+               : "memory");
+  return old;
+}
+
 // Counts `cnt` freshly stored scores of `row` (one fence for the batch); the
 // warp whose count completes the row resets its counter and selects its top-k.
 __device__ __noinline__ void publish_scores(const SelectParams& p, int row, int cnt, int total, int lane) {
@@ -328,9 +347,11 @@ __global__ void __launch_bounds__(kBulkThreads, 1) csa_select_bulk_kernel(Select
   uint64_t* empty = full + kStages;
   StageMeta* meta = reinterpret_cast<StageMeta*>(empty + kStages);
   int* abort_flag = reinterpret_cast<int*>(meta + kStages);
+  unsigned* unit_cnt = reinterpret_cast<unsigned*>(abort_flag + 16);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t chunk_bytes = uint32_t(p.chunk) * D * sizeof(T);
 
+  if (threadIdx.x < kUnitSlots) unit_cnt[threadIdx.x] = 0u;
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       sm100::mbar_init(&full[s], 1);
@@ -351,6 +372,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) csa_select_bulk_kernel(Select
       // atomic's round trip overlaps the copies instead of stalling the ring.
       int u_next = static_cast<int>(atomicAdd(p.ticket, 1u));
       int cached_b = -1, cached_chunks = 0;
+      uint32_t units_issued = 0;
       for (;;) {
         const int u = u_next;
         if (u >= p.total_units) break;
@@ -372,11 +394,12 @@ __global__ void __launch_bounds__(kBulkThreads, 1) csa_select_bulk_kernel(Select
         }
         const char* src = static_cast<const char*>(p.k) + (size_t(row) * p.seq_len) * D * sizeof(T);
         const int c1 = min((r + 1) * p.unit, row_chunks);
+        const int unit_tag = int(units_issued++ % kUnitSlots) | ((c1 - r * p.unit) << 8);
         for (int c = r * p.unit; c < c1 && ok; ++c, ++it) {
           const int s = it % kStages;
           if (it >= kStages) ok = sm100::mbar_wait(&empty[s], ((it / kStages) - 1) & 1, abort_v);
           if (!ok) break;
-          meta[s] = StageMeta{row, c, row_chunks, 0};
+          meta[s] = StageMeta{row, c, row_chunks, unit_tag};
           mbar_arrive_expect_tx(&full[s], chunk_bytes);
           bulk_g2s(sm100::smem_u32(stages + s * kStageBytes), src + size_t(c) * chunk_bytes, chunk_bytes, &full[s]);
         }
@@ -406,7 +429,6 @@ __global__ void __launch_bounds__(kBulkThreads, 1) csa_select_bulk_kernel(Select
     const int tok_lane = lane / G::kLPT, vec_lane = lane % G::kLPT;
     constexpr int kRowBytes = D * sizeof(T);
     int cached_row = -1;
-    int pend_row = -1, pend_cnt = 0, pend_total = 0;  // scores stored but not yet counted
     float qf[G::kFPL];
     for (uint32_t it = warp;; it += kBulkWarps) {
       const int s = it % kStages;
@@ -415,12 +437,6 @@ __global__ void __launch_bounds__(kBulkThreads, 1) csa_select_bulk_kernel(Select
         break;
       }
       const StageMeta m = meta[s];
-      if (m.row != pend_row) {  // publish the finished run of the previous row (or the last one)
-        if (pend_cnt > 0) publish_scores(p, pend_row, pend_cnt, pend_total, lane);
-        pend_row = m.row;
-        pend_total = m.row_chunks;
-        pend_cnt = 0;
-      }
       if (m.row < 0) break;
       if (m.row != cached_row) {
         const T* qrow = static_cast<const T*>(p.q) + size_t(m.row) * D;
@@ -458,8 +474,15 @@ __global__ void __launch_bounds__(kBulkThreads, 1) csa_select_bulk_kernel(Select
         dot = fmaf(qf[e], __fdiv_rn(sum, count), dot);
       }
       dot = warp_sum_xor(dot, 1, G::kLPT);
-      if (lane == 0) p.scores[size_t(m.row) * p.num_chunks + m.chunk] = dot * p.scale;
-      ++pend_cnt;
+      int unit_done = 0;
+      if (lane == 0) {
+        p.scores[size_t(m.row) * p.num_chunks + m.chunk] = dot * p.scale;
+        const int slot = m.unit & 0xFF, n = m.unit >> 8;
+        // Release the score to the warp that finishes the unit (same CTA).
+        unit_done = atom_add_acq_rel_cta(unit_cnt + slot, 1u) == unsigned(n - 1);
+        if (unit_done) unit_cnt[slot] = 0u;
+      }
+      if (__shfl_sync(0xffffffffu, unit_done, 0)) publish_scores(p, m.row, m.unit >> 8, m.row_chunks, lane);
     }
   }
 }
