@@ -322,6 +322,26 @@ def bench_mini_block(dev) -> dict:
     return res
 
 
+def bench_splitkv(dev, rank: int, world: int, steps: int, warmup: int) -> dict:
+    """One config-5 request (H64, 65536 context, 512 main + 64 C4 slots) decoded
+    with its slots split across the ranks: per-shard partial kernel, NCCL
+    all-gather of (o, lse), combine kernel.  Every rank holds the full caches.
+    Device time per step, max over ranks; L2 flushed before every step."""
+    from csahca_b200 import workloads as W
+    from csahca_b200.split_kv import dsv4_split_kv_decode
+
+    b = W.dsv4_cache(dev, num_queries=1, heads=64, context=65536, ratio=4, n_main=512, n_extra=64, seed=7)
+    fn = lambda: dsv4_split_kv_decode(  # noqa: E731
+        b.q, b.cache, b.token_indices, b.topk_lengths, b.extra_cache, b.extra_token_indices, b.extra_topk_lengths,
+        b.attn_sink, b.page_size, b.extra_page_size, b.softmax_scale)
+    _barrier(world)
+    ms = _max_over_ranks(_time_flushed(fn, dev, iters=steps, warm=warmup), dev, world)
+    return {"workload": "dsv4_splitkv (config 5 C4, one request, H64, 512 + 64 slots)", "n_gpus": world,
+            "us_per_step": round(ms * 1e3, 2), "steps": steps, "warmup": warmup,
+            "collective": "all_gather (o, lse) over NCCL" if world > 1 else "none",
+            "note": "latency-bound by design: one query's work is split, the exchange is one all-gather"}
+
+
 DSV4_CASES = {
     "dsv4_c0 (config 4: Q128 H64 window 128, ctx 2048-16384)":
         dict(num_queries=128, heads=64, context=(2048, 16384), ratio=0, window=128),
@@ -400,8 +420,10 @@ def main() -> int:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--cpu-requests", type=int, default=8, help="requests in one CPU-oracle sample")
-    ap.add_argument("--workload", choices=["csa_batched", "dsv4_c0", "dsv4_c4", "dsv4_c128"], default="csa_batched",
-                    help="dsv4_*: time only that DSV4 case (profiling / diagnosis); prints kernel timings")
+    ap.add_argument("--workload", choices=["csa_batched", "dsv4_c0", "dsv4_c4", "dsv4_c128", "dsv4_splitkv"],
+                    default="csa_batched",
+                    help="dsv4_c*: time only that DSV4 case (profiling / diagnosis); dsv4_splitkv: one config-5 "
+                         "request (C4) split across the ranks with an NCCL all-gather")
     ap.add_argument("--batch", type=int, default=64, help="csa_batched: override the batch (profiling only)")
     ap.add_argument("--queries", type=int, default=0, help="dsv4_*: override the number of queries")
     ap.add_argument("--context", type=int, default=0, help="dsv4_c4/c128: override the per-request context")
@@ -436,6 +458,13 @@ def main() -> int:
         torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local))
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    if a.workload == "dsv4_splitkv":
+        res = bench_splitkv(dev, rank, world, a.steps, max(3, a.warmup))
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return 0
     if a.workload != "csa_batched":
         kw = dict(next(v for k, v in DSV4_CASES.items() if k.startswith(a.workload)))
         if a.queries:

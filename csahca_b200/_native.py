@@ -55,6 +55,14 @@ def _declare(lib: ctypes.CDLL) -> None:
         _vp, _i64, _vp,                 # extra indices, extra slots, extra lengths
         _vp, ctypes.c_float, _vp, _vp,  # sink, scale, out, stream
     ]
+    lib.csahca_dsv4_decode_partial.restype = _int
+    lib.csahca_dsv4_decode_partial.argtypes = [
+        _vp, _int, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _vp,
+        _vp, _i64, _i64, _i64, _vp, _i64, _vp,
+        ctypes.c_float, _vp, _vp, _vp,  # scale, o_partial, lse_partial, stream
+    ]
+    lib.csahca_dsv4_combine_partials.restype = _int
+    lib.csahca_dsv4_combine_partials.argtypes = [_vp, _vp, _i64, _i64, _i64, _vp, _vp, _int, _vp]
 
 
 def lib() -> ctypes.CDLL:

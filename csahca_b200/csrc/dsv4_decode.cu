@@ -126,6 +126,7 @@ struct Dsv4Params {
   const int32_t* xlens;
   const float* sink;
   void* out;
+  float* lse;  // non-null: split-KV partial mode (fp32 o normalised by its own sum, lse in log2 units, no sink)
   int* err;
   int64_t bpp, xbpp;
   int64_t capacity, xcapacity;  // slots addressable in each cache
@@ -803,9 +804,11 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
       const int q = item / p.groups, hg = item - q * p.groups;
       if (slot_space(p, q).blocks() != 0) continue;
       const int hcount = min(kHeads, p.heads - hg * kHeads);
-      uint8_t* out_q = static_cast<uint8_t*>(p.out) + (size_t(q) * p.heads + size_t(hg) * kHeads) * kDim * esz;
-      const int nvec = hcount * kDim * esz / 16;
+      const int oesz = p.lse != nullptr ? 4 : esz;
+      uint8_t* out_q = static_cast<uint8_t*>(p.out) + (size_t(q) * p.heads + size_t(hg) * kHeads) * kDim * oesz;
+      const int nvec = hcount * kDim * oesz / 16;
       for (int i = t; i < nvec; i += 128) reinterpret_cast<uint4*>(out_q)[i] = make_uint4(0, 0, 0, 0);
+      if (p.lse != nullptr && t < hcount) p.lse[size_t(q) * p.heads + hg * kHeads + t] = -INFINITY;
     }
     // This lane's partial sums of P per head (in the m_use frame) live in TMEM
     // columns kTmemL .. kTmemL+63 until the query ends.
@@ -925,7 +928,8 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
       // -------------------------------------------------------------- epilogue
       const int q = cur.item / p.groups, hg = cur.item - q * p.groups;
       const int hcount = min(kHeads, p.heads - hg * kHeads);
-      uint8_t* out_q = static_cast<uint8_t*>(p.out) + (size_t(q) * p.heads + size_t(hg) * kHeads) * kDim * esz;
+      const int oesz = p.lse != nullptr ? 4 : esz;
+      uint8_t* out_q = static_cast<uint8_t*>(p.out) + (size_t(q) * p.heads + size_t(hg) * kHeads) * kDim * oesz;
       {
         // Per-head sums: reduce the lanes' partials once per query.
         float la[64];
@@ -948,7 +952,10 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
       if (t < kHeads) {
         float total = bars->red[0][t] + bars->red[1][t] + bars->red[2][t] + bars->red[3][t];
         const float mu = bars->m_use[t];
-        if (p.sink != nullptr && hg * kHeads + t < p.heads) {
+        if (p.lse != nullptr) {
+          if (hg * kHeads + t < p.heads)
+            p.lse[size_t(q) * p.heads + hg * kHeads + t] = (total > 0.f && mu != -INFINITY) ? mu + log2f(total) : -INFINITY;
+        } else if (p.sink != nullptr && hg * kHeads + t < p.heads) {
           const float sk = p.sink[hg * kHeads + t] * kLog2e;
           total += (mu == -INFINITY) ? (sk == -INFINITY ? 0.f : INFINITY) : exp2f(sk - mu);
         }
@@ -974,7 +981,13 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
             const int h = odd ? 2 * j + 1 : 2 * j;
             const float lo = odd ? recv : a0;
             const float hi = odd ? a1 : recv;
-            if (h < hcount) store_pair(reinterpret_cast<QT*>(out_q) + size_t(h) * kDim + (odd ? d - 1 : d), lo, hi);
+            if (h < hcount) {
+              const size_t e = size_t(h) * kDim + (odd ? d - 1 : d);
+              if (p.lse != nullptr)
+                store_pair(reinterpret_cast<float*>(out_q) + e, lo, hi);
+              else
+                store_pair(reinterpret_cast<QT*>(out_q) + e, lo, hi);
+            }
           }
         }
       }
@@ -1025,13 +1038,13 @@ int launch_dsv4(const Dsv4Params& p, cudaStream_t stream) {
 
 using namespace csahca;
 
-extern "C" int csahca_dsv4_decode(const void* q, int q_dtype, int64_t num_queries, int64_t heads, const uint8_t* cache,
-                                  int64_t num_pages, int64_t bytes_per_page, int64_t page_size,
-                                  const int32_t* token_indices, int64_t topk_slots, const int32_t* topk_lengths,
-                                  const uint8_t* extra_cache, int64_t extra_num_pages, int64_t extra_bytes_per_page,
-                                  int64_t extra_page_size, const int32_t* extra_token_indices,
-                                  int64_t extra_topk_slots, const int32_t* extra_topk_lengths, const float* attn_sink,
-                                  float softmax_scale, void* out, void* stream) {
+static int dsv4_entry(const void* q, int q_dtype, int64_t num_queries, int64_t heads, const uint8_t* cache,
+                      int64_t num_pages, int64_t bytes_per_page, int64_t page_size, const int32_t* token_indices,
+                      int64_t topk_slots, const int32_t* topk_lengths, const uint8_t* extra_cache,
+                      int64_t extra_num_pages, int64_t extra_bytes_per_page, int64_t extra_page_size,
+                      const int32_t* extra_token_indices, int64_t extra_topk_slots,
+                      const int32_t* extra_topk_lengths, const float* attn_sink, float softmax_scale, void* out,
+                      float* lse, void* stream) {
   if (page_size <= 0) return csahca_set_arg_error("page_size must be positive");
   if (num_queries < 0 || heads < 0 || topk_slots < 0 || num_pages < 0)
     return csahca_set_arg_error("sizes must be non-negative");
@@ -1061,8 +1074,9 @@ extern "C" int csahca_dsv4_decode(const void* q, int q_dtype, int64_t num_querie
   p.xcache = has_extra ? extra_cache : nullptr;
   p.xidx = has_extra ? extra_token_indices : nullptr;
   p.xlens = has_extra ? extra_topk_lengths : nullptr;
-  p.sink = attn_sink;
+  p.sink = lse != nullptr ? nullptr : attn_sink;
   p.out = out;
+  p.lse = lse;
   p.err = csahca_device_error_ptr();
   p.bpp = bytes_per_page;
   p.xbpp = has_extra ? extra_bytes_per_page : 0;
@@ -1084,6 +1098,34 @@ extern "C" int csahca_dsv4_decode(const void* q, int q_dtype, int64_t num_querie
     case CSAHCA_DTYPE_F32: return launch_dsv4<float>(p, s);
     default: return csahca_set_arg_error("unsupported q dtype");
   }
+}
+
+extern "C" int csahca_dsv4_decode(const void* q, int q_dtype, int64_t num_queries, int64_t heads, const uint8_t* cache,
+                                  int64_t num_pages, int64_t bytes_per_page, int64_t page_size,
+                                  const int32_t* token_indices, int64_t topk_slots, const int32_t* topk_lengths,
+                                  const uint8_t* extra_cache, int64_t extra_num_pages, int64_t extra_bytes_per_page,
+                                  int64_t extra_page_size, const int32_t* extra_token_indices,
+                                  int64_t extra_topk_slots, const int32_t* extra_topk_lengths, const float* attn_sink,
+                                  float softmax_scale, void* out, void* stream) {
+  return dsv4_entry(q, q_dtype, num_queries, heads, cache, num_pages, bytes_per_page, page_size, token_indices,
+                    topk_slots, topk_lengths, extra_cache, extra_num_pages, extra_bytes_per_page, extra_page_size,
+                    extra_token_indices, extra_topk_slots, extra_topk_lengths, attn_sink, softmax_scale, out, nullptr,
+                    stream);
+}
+
+extern "C" int csahca_dsv4_decode_partial(const void* q, int q_dtype, int64_t num_queries, int64_t heads,
+                                          const uint8_t* cache, int64_t num_pages, int64_t bytes_per_page,
+                                          int64_t page_size, const int32_t* token_indices, int64_t topk_slots,
+                                          const int32_t* topk_lengths, const uint8_t* extra_cache,
+                                          int64_t extra_num_pages, int64_t extra_bytes_per_page,
+                                          int64_t extra_page_size, const int32_t* extra_token_indices,
+                                          int64_t extra_topk_slots, const int32_t* extra_topk_lengths,
+                                          float softmax_scale, float* o_partial, float* lse_partial, void* stream) {
+  if (lse_partial == nullptr || o_partial == nullptr) return csahca_set_arg_error("o_partial and lse_partial are required");
+  return dsv4_entry(q, q_dtype, num_queries, heads, cache, num_pages, bytes_per_page, page_size, token_indices,
+                    topk_slots, topk_lengths, extra_cache, extra_num_pages, extra_bytes_per_page, extra_page_size,
+                    extra_token_indices, extra_topk_slots, extra_topk_lengths, nullptr, softmax_scale, o_partial,
+                    lse_partial, stream);
 }
 
 #ifdef CSAHCA_DSV4_TRACE

@@ -148,6 +148,33 @@ int csahca_dsv4_decode(const void* q, int q_dtype, int64_t num_queries, int64_t 
                        const int32_t* extra_topk_lengths, const float* attn_sink, float softmax_scale, void* out,
                        void* stream);
 
+/* ------------------------------------------------------------------ DSV4 split-KV
+ * One shard of a long request's slot list, and the merge of all shards.
+ * The reference has no host entry for this (its single-GPU merge is
+ * csrc/dsv4_attention.cu:273-335, dsv4_decode_merge_kernel, whose rule the
+ * combine follows); it serves the split-KV decode of one long request across
+ * GPUs, where each GPU decodes a contiguous range of the main and extra slots
+ * and the shards' (o, lse) are all-gathered and merged.
+ *
+ * csahca_dsv4_decode_partial: arguments as csahca_dsv4_decode without the
+ * sink; o_partial fp32 [Q,H,512] = the shard's output normalised by its own
+ * softmax sum; lse_partial fp32 [Q,H] = max score + log2(sum), in log2 units
+ * (scores already scaled by softmax_scale), -inf for a shard with no valid slot.
+ *
+ * csahca_dsv4_combine_partials: o_parts [parts,Q,H,512] and lse_parts
+ * [parts,Q,H] (fp32, shard-major) -> out [Q,H,512] of out_dtype; attn_sink NULL
+ * or fp32 [H], counted once as a zero-valued token.  1 <= parts <= 64.
+ */
+int csahca_dsv4_decode_partial(const void* q, int q_dtype, int64_t num_queries, int64_t heads, const uint8_t* cache,
+                               int64_t num_pages, int64_t bytes_per_page, int64_t page_size,
+                               const int32_t* token_indices, int64_t topk_slots, const int32_t* topk_lengths,
+                               const uint8_t* extra_cache, int64_t extra_num_pages, int64_t extra_bytes_per_page,
+                               int64_t extra_page_size, const int32_t* extra_token_indices, int64_t extra_topk_slots,
+                               const int32_t* extra_topk_lengths, float softmax_scale, float* o_partial,
+                               float* lse_partial, void* stream);
+int csahca_dsv4_combine_partials(const float* o_parts, const float* lse_parts, int64_t parts, int64_t num_queries,
+                                 int64_t heads, const float* attn_sink, void* out, int out_dtype, void* stream);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

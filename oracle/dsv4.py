@@ -12,6 +12,9 @@ Follows hybrid_attention/dsv4_correctness.py:
 * ``reference_attention``:91-141 (fp32 softmax with the sink as a zero-valued
                                   virtual token; lengths clamped to [0, slots];
                                   negative slots skipped)
+* ``partial_attention`` / ``combine_partials``: the same decode split over
+  shards of the slot list and merged by log-sum-exp, the sink entering once
+  (the merge rule of csrc/dsv4_attention.cu:273-335)
 
 The slot-validity rules match csrc/dsv4_attention.cu:185-225.
 """
@@ -163,3 +166,64 @@ def reference_attention(
 
 def default_softmax_scale() -> float:
     return 1.0 / math.sqrt(HEAD_DIM)
+
+
+def partial_attention(
+    q: np.ndarray,
+    q_dtype: str,
+    cache: np.ndarray,
+    token_indices: np.ndarray,
+    topk_lengths: np.ndarray | None,
+    *,
+    page_size: int,
+    softmax_scale: float,
+    extra_cache: np.ndarray | None = None,
+    extra_token_indices: np.ndarray | None = None,
+    extra_topk_lengths: np.ndarray | None = None,
+    extra_page_size: int | None = None,
+) -> tuple[np.ndarray, np.ndarray]:
+    """One shard of a split-KV decode: softmax over this shard's valid slots only,
+    no sink.  Returns ``(o, lse)``: fp32 ``[Q,H,512]`` normalised by the shard's
+    own sum, and fp32 ``[Q,H]`` = log2 of that sum plus the max score in log2
+    units (``-inf`` for a shard with no valid slot, whose ``o`` is zero)."""
+    nq, heads, _ = q.shape
+    qf = to_f32(q, q_dtype)
+    scale = np.float32(softmax_scale)
+    o = np.zeros((nq, heads, HEAD_DIM), np.float32)
+    lse = np.full((nq, heads), -np.inf, np.float32)
+    for qi in range(nq):
+        main = _valid_slots(token_indices[qi], None if topk_lengths is None else topk_lengths[qi])
+        rows = [dequant_dsv4_cache(cache, main, page_size=page_size)] if main.size else []
+        if extra_cache is not None and extra_token_indices is not None and extra_token_indices.shape[1] > 0:
+            xs = _valid_slots(extra_token_indices[qi], None if extra_topk_lengths is None else extra_topk_lengths[qi])
+            if xs.size:
+                rows.append(dequant_dsv4_cache(extra_cache, xs, page_size=extra_page_size))
+        if not rows:
+            continue
+        kv = bf16_to_f32(np.concatenate(rows, axis=0))
+        scores = (kv @ qf[qi].T).astype(np.float32) * scale  # [N, H]
+        m = scores.max(axis=0)
+        e = np.exp(scores - m[None, :], dtype=np.float32)
+        s = e.sum(axis=0, dtype=np.float32)
+        o[qi] = (e / s[None, :]).T @ kv
+        lse[qi] = (np.log2(s) + m * np.float32(math.log2(math.e))).astype(np.float32)
+    return o, lse
+
+
+def combine_partials(o_parts: np.ndarray, lse_parts: np.ndarray, attn_sink: np.ndarray | None,
+                     q_dtype: str) -> np.ndarray:
+    """Merge shard outputs ``[G,Q,H,512]`` / ``[G,Q,H]`` into the full decode,
+    the sink entering once as a zero-valued token (dsv4_attention.cu:292-299)."""
+    lse = lse_parts.astype(np.float64)
+    m = lse.max(axis=0)
+    if attn_sink is not None:
+        sk = np.asarray(attn_sink, np.float64)[None, :] * math.log2(math.e)
+        m = np.maximum(m, sk)
+    with np.errstate(invalid="ignore"):
+        w = np.where(np.isfinite(lse), np.exp2(lse - m[None]), 0.0)
+    total = w.sum(axis=0)
+    if attn_sink is not None:
+        total = total + np.where(np.isfinite(m), np.exp2(sk - m), 0.0)
+    out = (w[..., None] * o_parts).sum(axis=0) / np.where(total > 0, total, 1.0)[..., None]
+    out = np.where((total > 0)[..., None], out, 0.0)
+    return from_f32(out.astype(np.float32), q_dtype)
