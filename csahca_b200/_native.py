@@ -59,7 +59,7 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.csahca_dsv4_decode_partial.argtypes = [
         _vp, _int, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _vp,
         _vp, _i64, _i64, _i64, _vp, _i64, _vp,
-        ctypes.c_float, _vp, _vp, _vp,  # scale, o_partial, lse_partial, stream
+        ctypes.c_float, _i64, _i64, _i64, _vp, _vp, _vp,  # scale, shard0, shards, total, o, lse, stream
     ]
     lib.csahca_dsv4_combine_partials.restype = _int
     lib.csahca_dsv4_combine_partials.argtypes = [_vp, _vp, _i64, _i64, _i64, _vp, _vp, _int, _vp]

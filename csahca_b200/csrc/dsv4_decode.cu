@@ -133,6 +133,11 @@ struct Dsv4Params {
   int page, xpage;
   int nmain, nextra;  // slots per query in each index list
   int num_queries, heads, groups, num_items;
+  // Slot-list sharding (split-KV): this launch decodes shards split0 ..
+  // split0+splits-1 of split_total equal ranges of every query's main and
+  // extra slot lists; work row qs = s * num_queries + q (s local), and the
+  // outputs are indexed by qs.  splits = split_total = 1 for a plain decode.
+  int splits, split0, split_total;
   float scale_log2;
 };
 
@@ -152,23 +157,34 @@ struct Bars {
 };
 static_assert(sizeof(Bars) <= kBarBytes, "barrier area too large");
 
-// Valid-slot space of a query: main slots then extra slots.
+// Valid-slot space of one work row (a query, or one shard of a query's slot
+// lists): main slots then extra slots, starting at main_off / extra_off of the
+// query's index lists.
 struct SlotSpace {
-  int len_main, len_extra;
+  int q;  // the query
+  int len_main, len_extra, main_off, extra_off;
   __device__ __forceinline__ int total() const { return len_main + len_extra; }
   __device__ __forceinline__ int blocks() const { return (total() + kSlots - 1) / kSlots; }
 };
 
-__device__ __forceinline__ SlotSpace slot_space(const Dsv4Params& p, int q) {
+__device__ __forceinline__ SlotSpace slot_space(const Dsv4Params& p, int qs) {
   SlotSpace s;
-  const int lm = p.lens != nullptr ? p.lens[q] : p.nmain;
-  s.len_main = max(0, min(lm, p.nmain));
-  int lx = 0;
+  s.q = qs % p.num_queries;
+  const int sg = p.split0 + qs / p.num_queries;
+  const int lm = max(0, min(p.lens != nullptr ? p.lens[s.q] : p.nmain, p.nmain));
+  const int lo_m = int((int64_t(p.nmain) * sg) / p.split_total);
+  const int hi_m = int((int64_t(p.nmain) * (sg + 1)) / p.split_total);
+  s.main_off = lo_m;
+  s.len_main = max(0, min(lm - lo_m, hi_m - lo_m));
+  s.len_extra = 0;
+  s.extra_off = 0;
   if (p.xcache != nullptr && p.xidx != nullptr && p.nextra > 0) {
-    lx = p.xlens != nullptr ? p.xlens[q] : p.nextra;
-    lx = max(0, min(lx, p.nextra));
+    const int lx = max(0, min(p.xlens != nullptr ? p.xlens[s.q] : p.nextra, p.nextra));
+    const int lo_x = int((int64_t(p.nextra) * sg) / p.split_total);
+    const int hi_x = int((int64_t(p.nextra) * (sg + 1)) / p.split_total);
+    s.extra_off = lo_x;
+    s.len_extra = max(0, min(lx - lo_x, hi_x - lo_x));
   }
-  s.len_extra = lx;
   return s;
 }
 
@@ -179,35 +195,7 @@ struct SlotEntry {
 };
 static_assert(sizeof(SlotEntry) == 16, "slot table entry is 16 bytes");
 
-// Threads 0..127 of the producer group each resolve one slot of block `blk` of
-// query q into `tab` (index load, 32-bit page arithmetic, scale-byte load).
-__device__ __forceinline__ void resolve_block(const Dsv4Params& p, const SlotSpace& sp, int q, int blk, int tid,
-                                              SlotEntry* tab) {
-  if (tid < 0 || tid >= kSlots) return;
-  SlotEntry e;
-  e.row = nullptr;
-  e.scales = make_uint2(0, 0);
-  const int gs = blk * kSlots + tid;
-  if (gs < sp.total()) {
-    const bool main = gs < sp.len_main;
-    const int loc = main ? __ldg(p.idx + size_t(q) * p.nmain + gs)
-                         : __ldg(p.xidx + size_t(q) * p.nextra + (gs - sp.len_main));
-    const int64_t cap = main ? p.capacity : p.xcapacity;
-    if (loc >= 0 && loc < cap) {
-      const unsigned page_size = unsigned(main ? p.page : p.xpage);
-      const unsigned page = unsigned(loc) / page_size;
-      const unsigned in_page = unsigned(loc) - page * page_size;
-      const uint8_t* pb = (main ? p.cache : p.xcache) + int64_t(page) * (main ? p.bpp : p.xbpp);
-      e.row = pb + int64_t(in_page) * kRowBytes;
-      e.scales = __ldg(reinterpret_cast<const uint2*>(pb + int64_t(page_size) * kRowBytes + int64_t(in_page) * kScaleBytes));
-    } else if (loc >= cap) {
-      report_device_error(p.err, kErrSlotOutOfRange);
-    }
-  }
-  tab[tid] = e;
-}
-
-// Split form of resolve_block for the producer pipeline: slot_loc() issues the
+// Slot resolution in two steps for the resolver pipeline: slot_loc() issues the
 // index load, finish_slot() turns the index into the row address and issues
 // the scale-byte load; the caller stores the entry one step later.
 struct PendingSlot {
@@ -215,14 +203,16 @@ struct PendingSlot {
   bool main;
 };
 
-__device__ __forceinline__ PendingSlot slot_loc(const Dsv4Params& p, const SlotSpace& sp, int q, int blk, int tid) {
+__device__ __forceinline__ PendingSlot slot_loc(const Dsv4Params& p, const SlotSpace& sp, int blk, int tid) {
+  const int q = sp.q;
   PendingSlot r;
   r.loc = -1;
   r.main = true;
   const int gs = blk * kSlots + tid;
   if (tid >= 0 && tid < kSlots && gs < sp.total()) {
     r.main = gs < sp.len_main;
-    r.loc = r.main ? __ldg(p.idx + size_t(q) * p.nmain + gs) : __ldg(p.xidx + size_t(q) * p.nextra + (gs - sp.len_main));
+    r.loc = r.main ? __ldg(p.idx + size_t(q) * p.nmain + sp.main_off + gs)
+                   : __ldg(p.xidx + size_t(q) * p.nextra + sp.extra_off + (gs - sp.len_main));
   }
   return r;
 }
@@ -638,9 +628,9 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
     PendingSlot ps;
     ps.loc = -1;
     ps.main = true;
-    if (c0.valid) e0 = finish_slot(p, slot_loc(p, c0.sp, c0.item / p.groups, c0.blk, rs));
-    if (c1.valid) e1 = finish_slot(p, slot_loc(p, c1.sp, c1.item / p.groups, c1.blk, rs));
-    if (c2.valid) ps = slot_loc(p, c2.sp, c2.item / p.groups, c2.blk, rs);
+    if (c0.valid) e0 = finish_slot(p, slot_loc(p, c0.sp, c0.blk, rs));
+    if (c1.valid) e1 = finish_slot(p, slot_loc(p, c1.sp, c1.blk, rs));
+    if (c2.valid) ps = slot_loc(p, c2.sp, c2.blk, rs);
     while (c0.valid) {
       const int tb = j % kTabBufs;
       if (j >= kTabBufs && !(ok = mbar_wait(&bars->tab_empty[tb], ((j / kTabBufs) - 1) & 1, abort_flag))) break;
@@ -649,7 +639,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
       const Cursor c3 = next_cursor(p, c2);
       e0 = e1;
       if (c2.valid) e1 = finish_slot(p, ps);
-      if (c3.valid) ps = slot_loc(p, c3.sp, c3.item / p.groups, c3.blk, rs);
+      if (c3.valid) ps = slot_loc(p, c3.sp, c3.blk, rs);
       c0 = c1;
       c1 = c2;
       c2 = c3;
@@ -663,8 +653,10 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
     bool ok = true;
     uint32_t items = 0;
     for (int it = blockIdx.x; it < p.num_items && ok; it += gridDim.x) {
-      const int q = it / p.groups, hg = it - q * p.groups;
-      if (slot_space(p, q).blocks() == 0) continue;
+      const int qs = it / p.groups, hg = it - qs * p.groups;
+      const SlotSpace sp = slot_space(p, qs);
+      if (sp.blocks() == 0) continue;
+      const int q = sp.q;
       if (items > 0 && !(ok = mbar_wait(&bars->q_empty, (items - 1) & 1, abort_flag))) break;
       const QT* qsrc = static_cast<const QT*>(p.q) + size_t(q) * p.heads * kDim;
 #pragma unroll 4
@@ -801,7 +793,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
     constexpr int esz = sizeof(QT);
     // Items without any valid slot: zeros (the sink alone gives a zero output).
     for (int item = blockIdx.x; item < p.num_items; item += gridDim.x) {
-      const int q = item / p.groups, hg = item - q * p.groups;
+      const int q = item / p.groups, hg = item - q * p.groups;  // q: work row (query-shard)
       if (slot_space(p, q).blocks() != 0) continue;
       const int hcount = min(kHeads, p.heads - hg * kHeads);
       const int oesz = p.lse != nullptr ? 4 : esz;
@@ -926,7 +918,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
       if (cur.blk != cur.nblk - 1) continue;
 
       // -------------------------------------------------------------- epilogue
-      const int q = cur.item / p.groups, hg = cur.item - q * p.groups;
+      const int q = cur.item / p.groups, hg = cur.item - q * p.groups;  // q: work row (query-shard)
       const int hcount = min(kHeads, p.heads - hg * kHeads);
       const int oesz = p.lse != nullptr ? 4 : esz;
       uint8_t* out_q = static_cast<uint8_t*>(p.out) + (size_t(q) * p.heads + size_t(hg) * kHeads) * kDim * oesz;
@@ -964,32 +956,46 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
       }
       named_bar_sync(1, 128);
       {
-        // Lane pairs (dims d, d+1) swap halves so each lane stores 2 adjacent dims
-        // of one head: a warp store covers two 64-byte runs of two head rows.
-        const bool odd = (lane & 1) != 0;
-        for (int m = 0; m < 4; ++m) {
-          float o[64];
-          tmem_ld32(t_lane + 64 * m, o);
-          tmem_ld32(t_lane + 64 * m + 32, o + 32);
-          tmem_wait_ld();
-          const int d = 128 * m + t;  // this lane's dim
+        // Stage rounds of heads in the (free) P buffers as [head][512] rows of
+        // the output type -- each thread owns one dim of each O^T block -- and
+        // send every round to global memory with one bulk store.
+        const bool f32out = p.lse != nullptr || esz == 4;
+        const int per_round = f32out ? 8 : 16;  // 16 KB of staging per round
+        const int oes = f32out ? 4 : esz;
+        for (int h0 = 0; h0 < hcount; h0 += per_round) {
+          if (h0 > 0) {
+            if (t == 0) bulk_wait_read_all();
+            named_bar_sync(1, 128);  // the previous round's bulk store has read the staging
+          }
+          for (int m = 0; m < 4; ++m) {
+            float o[16];
+            tmem_ld16(t_lane + 64 * m + h0, o);
+            tmem_wait_ld();
+            const int d = 128 * m + t;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float a0 = o[2 * j] * bars->inv_l[2 * j];
-            const float a1 = o[2 * j + 1] * bars->inv_l[2 * j + 1];
-            const float recv = __shfl_xor_sync(0xffffffffu, odd ? a0 : a1, 1);
-            const int h = odd ? 2 * j + 1 : 2 * j;
-            const float lo = odd ? recv : a0;
-            const float hi = odd ? a1 : recv;
-            if (h < hcount) {
-              const size_t e = size_t(h) * kDim + (odd ? d - 1 : d);
-              if (p.lse != nullptr)
-                store_pair(reinterpret_cast<float*>(out_q) + e, lo, hi);
-              else
-                store_pair(reinterpret_cast<QT*>(out_q) + e, lo, hi);
+            for (int i = 0; i < 16; ++i) {
+              if (i < per_round) {
+                const float v = o[i] * bars->inv_l[h0 + i];
+                const uint32_t a = p_base + uint32_t((i * kDim + d) * oes);
+                if (f32out)
+                  asm volatile("st.shared.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
+                else {
+                  const QT x = Elem<QT>::from_f(v);
+                  asm volatile("st.shared.u16 [%0], %1;" ::"r"(a), "h"(*reinterpret_cast<const unsigned short*>(&x))
+                               : "memory");
+                }
+              }
             }
           }
+          fence_proxy_async_smem();
+          named_bar_sync(1, 128);
+          if (t == 0) {
+            const int nh = min(per_round, hcount - h0);
+            bulk_store_s2g(out_q + size_t(h0) * kDim * oes, p_base, uint32_t(nh * kDim * oes));
+            bulk_commit();
+          }
         }
+        if (t == 0) bulk_wait_read_all();  // the P buffers are free again for the next query
       }
       tc_fence_before();
       if (t == 0) DSV4_TRACE(items_done, 0, 11);
@@ -1044,7 +1050,9 @@ static int dsv4_entry(const void* q, int q_dtype, int64_t num_queries, int64_t h
                       int64_t extra_num_pages, int64_t extra_bytes_per_page, int64_t extra_page_size,
                       const int32_t* extra_token_indices, int64_t extra_topk_slots,
                       const int32_t* extra_topk_lengths, const float* attn_sink, float softmax_scale, void* out,
-                      float* lse, void* stream) {
+                      float* lse, int64_t shard0, int64_t shards, int64_t shards_total, void* stream) {
+  if (shards < 1 || shards_total < 1 || shard0 < 0 || shard0 + shards > shards_total)
+    return csahca_set_arg_error("invalid shard range");
   if (page_size <= 0) return csahca_set_arg_error("page_size must be positive");
   if (num_queries < 0 || heads < 0 || topk_slots < 0 || num_pages < 0)
     return csahca_set_arg_error("sizes must be non-negative");
@@ -1064,7 +1072,7 @@ static int dsv4_entry(const void* q, int q_dtype, int64_t num_queries, int64_t h
     return csahca_set_unsupported("extra paged cache base and bytes_per_page must be multiples of 16 bytes");
   if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) & 15)
     return csahca_set_arg_error("q and out must be 16-byte aligned");
-  if (num_queries * heads > (int64_t(1) << 30)) return csahca_set_unsupported("problem too large");
+  if (num_queries * shards * heads > (int64_t(1) << 30)) return csahca_set_unsupported("problem too large");
 
   Dsv4Params p;
   p.q = q;
@@ -1089,7 +1097,10 @@ static int dsv4_entry(const void* q, int q_dtype, int64_t num_queries, int64_t h
   p.num_queries = int(num_queries);
   p.heads = int(heads);
   p.groups = int((heads + kHeads - 1) / kHeads);
-  p.num_items = p.num_queries * p.groups;
+  p.splits = int(shards);
+  p.split0 = int(shard0);
+  p.split_total = int(shards_total);
+  p.num_items = p.num_queries * p.splits * p.groups;
   p.scale_log2 = softmax_scale * kLog2e;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (q_dtype) {
@@ -1110,7 +1121,7 @@ extern "C" int csahca_dsv4_decode(const void* q, int q_dtype, int64_t num_querie
   return dsv4_entry(q, q_dtype, num_queries, heads, cache, num_pages, bytes_per_page, page_size, token_indices,
                     topk_slots, topk_lengths, extra_cache, extra_num_pages, extra_bytes_per_page, extra_page_size,
                     extra_token_indices, extra_topk_slots, extra_topk_lengths, attn_sink, softmax_scale, out, nullptr,
-                    stream);
+                    0, 1, 1, stream);
 }
 
 extern "C" int csahca_dsv4_decode_partial(const void* q, int q_dtype, int64_t num_queries, int64_t heads,
@@ -1120,12 +1131,13 @@ extern "C" int csahca_dsv4_decode_partial(const void* q, int q_dtype, int64_t nu
                                           int64_t extra_num_pages, int64_t extra_bytes_per_page,
                                           int64_t extra_page_size, const int32_t* extra_token_indices,
                                           int64_t extra_topk_slots, const int32_t* extra_topk_lengths,
-                                          float softmax_scale, float* o_partial, float* lse_partial, void* stream) {
+                                          float softmax_scale, int64_t shard0, int64_t shards, int64_t shards_total,
+                                          float* o_partial, float* lse_partial, void* stream) {
   if (lse_partial == nullptr || o_partial == nullptr) return csahca_set_arg_error("o_partial and lse_partial are required");
   return dsv4_entry(q, q_dtype, num_queries, heads, cache, num_pages, bytes_per_page, page_size, token_indices,
                     topk_slots, topk_lengths, extra_cache, extra_num_pages, extra_bytes_per_page, extra_page_size,
                     extra_token_indices, extra_topk_slots, extra_topk_lengths, nullptr, softmax_scale, o_partial,
-                    lse_partial, stream);
+                    lse_partial, shard0, shards, shards_total, stream);
 }
 
 #ifdef CSAHCA_DSV4_TRACE

@@ -4,7 +4,7 @@ One process per GPU.  Every rank holds the request's paged caches (or the pages
 its slots point to) and the same index lists; rank r of G decodes a contiguous
 range of the main slots and of the extra slots (``shard_slots``), producing an
 fp32 output normalised by its own softmax sum and its log-sum-exp
-(``dsv4_decode_partial``).  The (o, lse) pairs are all-gathered over the process
+(``dsv4_decode_partial``; the kernel slices the lists itself).  The (o, lse) pairs are all-gathered over the process
 group (NCCL over NVLink on a B200 node) and every rank merges them locally
 (``dsv4_combine_partials``), the sink counted once.  The merge rule is the
 reference's split merge (csrc/dsv4_attention.cu:273-335); the reference runs
@@ -16,6 +16,7 @@ The all-gather moves Q*H*(512+1)*4 bytes per rank (131 KB for one query with
 
 from __future__ import annotations
 
+import functools
 from typing import Callable
 
 import torch
@@ -49,31 +50,29 @@ def shard_slots(token_indices: torch.Tensor, topk_lengths: torch.Tensor | None, 
     return idx, lens
 
 
-def stack_shards(token_indices: torch.Tensor, topk_lengths: torch.Tensor | None, shards: range,
-                 total: int) -> tuple[torch.Tensor, torch.Tensor]:
-    """Slices ``shards`` (of ``total``) of an index list stacked shard-major as
-    extra queries: ``[len(shards) * Q, width]`` indices (short slices padded with
-    -1, which the kernel skips) and ``[len(shards) * Q]`` lengths."""
-    parts = [shard_slots(token_indices, topk_lengths, s, total) for s in shards]
-    width = max(p[0].shape[1] for p in parts)
-    idx = torch.cat([torch.nn.functional.pad(p[0], (0, width - p[0].shape[1]), value=-1) for p in parts])
-    return idx.contiguous(), torch.cat([p[1] for p in parts]).contiguous()
+@functools.lru_cache(maxsize=None)
+def _sm_count(device_index: int) -> int:
+    return torch.cuda.get_device_properties(device_index).multi_processor_count
 
 
 def auto_local_splits(num_queries: int, slots: int, device: torch.device) -> int:
     """Shards per GPU so that about one CTA per SM has work, at least 64 slots each."""
-    sms = torch.cuda.get_device_properties(device).multi_processor_count if device.type == "cuda" else 1
+    sms = _sm_count(device.index if device.index is not None else torch.cuda.current_device()) \
+        if device.type == "cuda" else 1
     return max(1, min(sms // max(1, num_queries), slots // 64))
 
 
 def dsv4_decode_partial(q, paged_k_cache_u8, token_indices, topk_lengths, extra_paged_k_cache_u8,
                         extra_token_indices, extra_topk_lengths, page_size: int, extra_page_size: int,
-                        softmax_scale: float) -> tuple[torch.Tensor, torch.Tensor]:
-    """One shard: ``(o fp32 [Q,H,512], lse fp32 [Q,H])`` on the B200 kernel."""
+                        softmax_scale: float, shard0: int = 0, shards: int = 1,
+                        shards_total: int = 1) -> tuple[torch.Tensor, torch.Tensor]:
+    """Shards ``shard0 .. shard0+shards-1`` of ``shards_total`` (equal ranges of
+    every query's main and extra slot lists, sliced inside the kernel) in one
+    launch: ``(o fp32 [shards,Q,H,512], lse fp32 [shards,Q,H])``."""
     lib = N.lib()
     nq, heads, _ = q.shape
-    o = torch.empty((nq, heads, DSV4_HEAD_DIM), dtype=torch.float32, device=q.device)
-    lse = torch.empty((nq, heads), dtype=torch.float32, device=q.device)
+    o = torch.empty((shards, nq, heads, DSV4_HEAD_DIM), dtype=torch.float32, device=q.device)
+    lse = torch.empty((shards, nq, heads), dtype=torch.float32, device=q.device)
     if nq == 0 or heads == 0:
         return o, lse
     x, xi, xl = extra_paged_k_cache_u8, extra_token_indices, extra_topk_lengths
@@ -87,7 +86,8 @@ def dsv4_decode_partial(q, paged_k_cache_u8, token_indices, topk_lengths, extra_
             x.data_ptr() if has_extra else None, x.shape[0] if has_extra else 0, x.shape[1] if has_extra else 0,
             int(extra_page_size) if has_extra else 1, xi.data_ptr() if has_extra else None,
             xi.shape[1] if has_extra else 0, N.ptr(xl) if has_extra else None,
-            float(softmax_scale), o.data_ptr(), lse.data_ptr(), N.stream_handle(q.device)))
+            float(softmax_scale), int(shard0), int(shards), int(shards_total), o.data_ptr(), lse.data_ptr(),
+            N.stream_handle(q.device)))
     return o, lse
 
 
@@ -114,34 +114,26 @@ def dsv4_split_kv_decode(q, paged_k_cache_u8, token_indices, topk_lengths, extra
     Every rank passes the same arguments and gets the full output.  With no
     initialised process group (or a group of one) only the local split applies.
     Each rank further splits its range into ``local_splits`` shards (default:
-    enough to give every SM work) that one partial launch decodes side by side
-    as extra queries, so a single long request spreads over the GPU's SMs too.
+    enough to give every SM work) that one partial launch decodes side by side,
+    so a single long request spreads over the GPU's SMs too.
     ``partial_fn`` / ``combine_fn`` replace the GPU kernels (the CPU tests run
-    the host logic and the collective with the numpy oracle in their place).
+    the host logic and the collective with the numpy oracle in their place);
+    ``partial_fn`` has the signature of ``dsv4_decode_partial``.
     """
     partial_fn = partial_fn or dsv4_decode_partial
     combine_fn = combine_fn or dsv4_combine_partials
     distributed = dist.is_available() and dist.is_initialized()
     world = dist.get_world_size(group) if distributed else 1
     rank = dist.get_rank(group) if distributed else 0
-    nq = q.shape[0]
     if local_splits is None:
-        local_splits = auto_local_splits(nq, token_indices.shape[1] // world, q.device)
+        local_splits = auto_local_splits(q.shape[0], token_indices.shape[1] // world, q.device)
     local_splits = max(1, int(local_splits))
-    total = world * local_splits
-    mine = range(rank * local_splits, (rank + 1) * local_splits)
-    idx, lens = stack_shards(token_indices, topk_lengths, mine, total)
     has_extra = (extra_paged_k_cache_u8 is not None and extra_token_indices is not None
                  and extra_token_indices.numel() > 0)
-    if has_extra:
-        xidx, xlens = stack_shards(extra_token_indices, extra_topk_lengths, mine, total)
-    else:
-        xidx = xlens = None
-    qs = q.repeat(local_splits, 1, 1) if local_splits > 1 else q
-    o, lse = partial_fn(qs, paged_k_cache_u8, idx, lens, extra_paged_k_cache_u8 if has_extra else None, xidx, xlens,
-                        page_size, extra_page_size, softmax_scale)
-    o = o.reshape((local_splits, nq) + tuple(o.shape[1:]))
-    lse = lse.reshape((local_splits, nq) + tuple(lse.shape[1:]))
+    o, lse = partial_fn(q, paged_k_cache_u8, token_indices, topk_lengths,
+                        extra_paged_k_cache_u8 if has_extra else None, extra_token_indices if has_extra else None,
+                        extra_topk_lengths if has_extra else None, page_size, extra_page_size, softmax_scale,
+                        rank * local_splits, local_splits, world * local_splits)
     if world > 1:
         o_all = torch.empty((world * o.shape[0],) + tuple(o.shape[1:]), dtype=o.dtype, device=o.device)
         lse_all = torch.empty((world * lse.shape[0],) + tuple(lse.shape[1:]), dtype=lse.dtype, device=lse.device)

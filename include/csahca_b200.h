@@ -157,9 +157,13 @@ int csahca_dsv4_decode(const void* q, int q_dtype, int64_t num_queries, int64_t 
  * and the shards' (o, lse) are all-gathered and merged.
  *
  * csahca_dsv4_decode_partial: arguments as csahca_dsv4_decode without the
- * sink; o_partial fp32 [Q,H,512] = the shard's output normalised by its own
- * softmax sum; lse_partial fp32 [Q,H] = max score + log2(sum), in log2 units
- * (scores already scaled by softmax_scale), -inf for a shard with no valid slot.
+ * sink, plus a shard range: every query's main and extra slot lists are cut
+ * into shards_total equal contiguous ranges (range s of n slots is
+ * [n*s/shards_total, n*(s+1)/shards_total), lengths clamped into it) and this
+ * call decodes shards shard0 .. shard0+shards-1, all in one launch.
+ * o_partial fp32 [shards,Q,H,512] = each shard's output normalised by its own
+ * softmax sum; lse_partial fp32 [shards,Q,H] = max score + log2(sum), in log2
+ * units (scores already scaled by softmax_scale), -inf for an empty shard.
  *
  * csahca_dsv4_combine_partials: o_parts [parts,Q,H,512] and lse_parts
  * [parts,Q,H] (fp32, shard-major) -> out [Q,H,512] of out_dtype; attn_sink NULL
@@ -170,8 +174,9 @@ int csahca_dsv4_decode_partial(const void* q, int q_dtype, int64_t num_queries, 
                                const int32_t* token_indices, int64_t topk_slots, const int32_t* topk_lengths,
                                const uint8_t* extra_cache, int64_t extra_num_pages, int64_t extra_bytes_per_page,
                                int64_t extra_page_size, const int32_t* extra_token_indices, int64_t extra_topk_slots,
-                               const int32_t* extra_topk_lengths, float softmax_scale, float* o_partial,
-                               float* lse_partial, void* stream);
+                               const int32_t* extra_topk_lengths, float softmax_scale, int64_t shard0,
+                               int64_t shards, int64_t shards_total, float* o_partial, float* lse_partial,
+                               void* stream);
 int csahca_dsv4_combine_partials(const float* o_parts, const float* lse_parts, int64_t parts, int64_t num_queries,
                                  int64_t heads, const float* attn_sink, void* out, int out_dtype, void* stream);
 

@@ -75,12 +75,20 @@ def _gloo_rank(rank, world, port, result_path):
     c = _golden()
     t = torch.from_numpy
 
-    def partial_fn(q, cache, idx, lens, xcache, xidx, xlens, page, xpage, scale):
-        o, lse = dsv4.partial_attention(q.numpy(), "bf16", cache.numpy(), idx.numpy(), lens.numpy(),
-                                        page_size=page, softmax_scale=scale, extra_cache=xcache.numpy(),
-                                        extra_token_indices=xidx.numpy(), extra_topk_lengths=xlens.numpy(),
-                                        extra_page_size=xpage)
-        return t(o), t(lse)
+    def partial_fn(q, cache, idx, lens, xcache, xidx, xlens, page, xpage, scale, shard0, shards, total):
+        from csahca_b200.split_kv import shard_slots
+
+        os_, ls_ = [], []
+        for sh in range(shard0, shard0 + shards):
+            i, li = shard_slots(idx, lens, sh, total)
+            xi, xli = shard_slots(xidx, xlens, sh, total)
+            o, lse = dsv4.partial_attention(q.numpy(), "bf16", cache.numpy(), i.numpy(), li.numpy(),
+                                            page_size=page, softmax_scale=scale, extra_cache=xcache.numpy(),
+                                            extra_token_indices=xi.numpy(), extra_topk_lengths=xli.numpy(),
+                                            extra_page_size=xpage)
+            os_.append(o)
+            ls_.append(lse)
+        return t(np.stack(os_)), t(np.stack(ls_))
 
     def combine_fn(o_all, lse_all, sink, dtype):
         return t(dsv4.combine_partials(o_all.numpy(), lse_all.numpy(), sink.numpy(), "bf16").astype(np.int16))
@@ -122,13 +130,24 @@ def test_gpu_partials_merge_to_full_decode(cuda, world):
     d = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
     q = to_torch(c["q"], "bf16", cuda)
     scale = 1.0 / math.sqrt(512)
-    parts = []
+    args = (q, d(c["cache"]), d(c["idx"]), d(c["tl"]), d(c["xcache"]), d(c["xidx"]), d(c["xl"]), page, xpage, scale)
+    parts = [dsv4_decode_partial(*args, r, 1, world) for r in range(world)]  # one shard per "rank"
+    o_all, lse_all = dsv4_decode_partial(*args, 0, world, world)  # all shards in one launch
+    torch.testing.assert_close(o_all, torch.cat([p[0] for p in parts]), atol=0, rtol=0)
+    torch.testing.assert_close(lse_all, torch.cat([p[1] for p in parts]), atol=0, rtol=0)
+    # the kernel's shard against the oracle's shard (host slicing)
     for r in range(world):
-        idx, tl = shard_slots(d(c["idx"]), d(c["tl"]), r, world)
-        xidx, xl = shard_slots(d(c["xidx"]), d(c["xl"]), r, world)
-        parts.append(dsv4_decode_partial(q, d(c["cache"]), idx, tl, d(c["xcache"]), xidx, xl, page, xpage, scale))
-    out = dsv4_combine_partials(torch.stack([p[0] for p in parts]), torch.stack([p[1] for p in parts]),
-                                d(c["sink"]), torch.bfloat16)
+        idx, tl = shard_slots(torch.from_numpy(c["idx"]), torch.from_numpy(c["tl"]), r, world)
+        xidx, xl = shard_slots(torch.from_numpy(c["xidx"]), torch.from_numpy(c["xl"]), r, world)
+        o_ref, lse_ref = dsv4.partial_attention(c["q"], "bf16", c["cache"], idx.numpy(), tl.numpy(), page_size=page,
+                                                softmax_scale=scale, extra_cache=c["xcache"],
+                                                extra_token_indices=xidx.numpy(), extra_topk_lengths=xl.numpy(),
+                                                extra_page_size=xpage)
+        np.testing.assert_allclose(parts[r][0][0].cpu().numpy(), o_ref, atol=ATOL, rtol=RTOL)
+        fin = np.isfinite(lse_ref)
+        np.testing.assert_array_equal(np.isfinite(parts[r][1][0].cpu().numpy()), fin)
+        np.testing.assert_allclose(parts[r][1][0].cpu().numpy()[fin], lse_ref[fin], atol=1e-3, rtol=1e-4)
+    out = dsv4_combine_partials(o_all, lse_all, d(c["sink"]), torch.bfloat16)
     full = ext.dsv4_sparse_decode_forward(q, d(c["cache"]), d(c["idx"]), d(c["tl"]), d(c["xcache"]), d(c["xidx"]),
                                           d(c["xl"]), d(c["sink"]), page, xpage, scale)
     ref = dsv4.reference_attention(c["q"], "bf16", c["cache"], c["idx"], c["tl"], c["sink"], page_size=page,
