@@ -54,26 +54,26 @@ constexpr int kRope = 64;
 constexpr int kDim = kNope + kRope;           // 512
 constexpr int kRowBytes = kNope + 2 * kRope;  // 576 data bytes per slot
 constexpr int kScaleBytes = 8;                // 7 UE8M0 scales + 1 pad per slot
-constexpr int kSlots = 128;                   // slots per block (MMA M of S^T)
+constexpr int kSlots = 64;                    // slots per block (MMA M of S^T)
 constexpr int kHeads = 64;                    // heads per CTA item (MMA N)
 
 constexpr int kSoftWarps = 4;
 constexpr int kMmaWarp = 4;
 constexpr int kProdWarp0 = 5;   // dequantising producers: 4 threads per slot row
 constexpr int kProdWarps = 8;
-constexpr int kProdThreads = kProdWarps * 32;  // 256: 4 threads per row pair (s, s + 64)
+constexpr int kProdThreads = kProdWarps * 32;  // 256 = kSlots x 4
 constexpr int kResWarp0 = kProdWarp0 + kProdWarps;  // slot-table resolvers: one thread per slot
 constexpr int kResWarps = 2;
-constexpr int kResThreads = kResWarps * 32;  // 64: slots rs and rs + 64
+constexpr int kResThreads = kResWarps * 32;  // 64 = kSlots
 constexpr int kQWarp = kResWarp0 + kResWarps;  // Q loader
 constexpr int kThreads = (kQWarp + 1) * 32;    // 512 (4 warps per sub-partition, 128 registers)
 
-constexpr int kKBufs = 1;                             // one K tile, refilled pair by pair behind PV
+constexpr int kKBufs = 2;                             // K tiles (and S / P buffers) in flight
 constexpr uint32_t kQBytes = kHeads * kDim * 2;      // 65536
-constexpr uint32_t kSubTileBytes = kSlots * 128;     // 16384: 128 slot rows x 64 dims bf16
-constexpr uint32_t kPairBytes = 2 * kSubTileBytes;   // 32768: dims 128m .. 128m+127
-constexpr uint32_t kBlockBytes = 4 * kPairBytes;     // 131072: one block's K tile
-constexpr uint32_t kPBytes = kSlots * kHeads * 2;    // 16384
+constexpr uint32_t kSubTileBytes = kSlots * 128;     // 8192: 64 slot rows x 64 dims bf16
+constexpr uint32_t kPairBytes = 2 * kSubTileBytes;   // 16384: dims 128m .. 128m+127
+constexpr uint32_t kBlockBytes = 4 * kPairBytes;     // 65536: one block's K tile
+constexpr uint32_t kPBytes = kSlots * kHeads * 2;    // 8192 per buffer
 constexpr uint32_t kOffQ = 0;
 constexpr uint32_t kOffK = kOffQ + kQBytes;
 constexpr uint32_t kOffP = kOffK + kKBufs * kBlockBytes;
@@ -81,12 +81,12 @@ constexpr uint32_t kOffBar = kOffP + kKBufs * kPBytes;
 constexpr int kTabBufs = 4;                                  // slot tables in flight (see resolvers)
 constexpr uint32_t kBarBytes = 2304;
 constexpr uint32_t kOffTab = kOffBar + kBarBytes;
-constexpr uint32_t kTabBytes = kTabBufs * kSlots * 16;      // 8 KB
+constexpr uint32_t kTabBytes = kTabBufs * kSlots * 16;      // 5 KB
 constexpr uint32_t kSmemBytes = kOffTab + kTabBytes + 1024;  // + alignment slack
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemS = 256;  // S^T (128 slot lanes x 64 heads) at column 256
+constexpr uint32_t kTmemS = 256;  // S^T buffers at columns 256 and 320
 constexpr uint32_t kTmemL = 384;  // per-lane running sums of P per head (64 columns)
 
 // Optional stage timestamps of CTA 0 (build with -DCSAHCA_DSV4_TRACE; diagnosis only).
@@ -506,19 +506,15 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
 
   if (warp >= kProdWarp0 && warp < kProdWarp0 + kProdWarps) {
     // ------------------------------------------------------------ producers
-    // Thread (s, r), s < 64, owns rows s and s + 64 of every block and, in each,
-    // the 16-byte chunks c = 4i + r (i = 0..8): chunks 0..27 are e4m3 (chunk
-    // 4i + r = dims 64i + 16r .. +15, scale group i, K sub-tile i), chunks 28..35
-    // the bf16 rope dims (K sub-tile 7).  Shared-memory offsets are per-thread
-    // constants (rows s and s + 64 share the swizzle phase); four threads read
-    // 64 contiguous bytes of a row.
-    // The K tile is refilled pair by pair (dims 128m .. 128m+127) as soon as PV
-    // of the previous block has read that pair.  Registers hold the next two
-    // pairs: `ev` the even pair (m = 0 / 2: 2 chunks x 2 rows), `od` the odd
-    // pair (m = 1: 2 x 2, m = 3: 3 x 2).  After storing pair 0 / 1 the loads of
-    // pair 2 / 3 go out into the same registers; after pair 3 those of pairs
-    // 0 and 1 of the next block.
-    // Invalid slots load nothing and store zeros.
+    // Thread (slot s, quarter r) owns 16-byte chunks c = 4i + r (i = 0..8) of
+    // slot row s in every block: chunks 0..27 are e4m3 (chunk 4i + r is dims
+    // 64i + 16r .. +15, scale group i, K sub-tile i), chunks 28..35 are the
+    // bf16 rope dims (K sub-tile 7).  The shared-memory offsets are therefore
+    // fixed per thread, and four threads read 64 contiguous bytes of a row.
+    // Block g goes to K buffer g%2.  One register set rotates pair by pair:
+    // right after the stores of pair m of block g, the loads of pair m of block
+    // g+1 go out into the same registers, so every row load has a block period
+    // to land.  Invalid slots load nothing and store zeros.
     const int pt = threadIdx.x - kProdWarp0 * 32;
     const int s = pt >> 2, r = pt & 3;
     const uint32_t x7 = uint32_t(s & 7), row_off = uint32_t(s) * 128u;
@@ -526,98 +522,91 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
     const uint32_t off_hi = row_off + ((uint32_t(2 * r + 1) ^ x7) << 4);
     const uint32_t off_r0 = 7u * kSubTileBytes + row_off + ((uint32_t(r) ^ x7) << 4);
     const uint32_t off_r1 = 7u * kSubTileBytes + row_off + ((uint32_t(r + 4) ^ x7) << 4);
-    constexpr uint32_t kRow64 = 64u * 128u;  // offset of row s + 64 in a sub-tile
-    uint4 ev[2][2], od[2][3];                // [row][chunk]
-    uint2 sc[2] = {make_uint2(0, 0), make_uint2(0, 0)};
+    uint4 raw[9];
+    uint2 sc = make_uint2(0, 0);
     bool ok = true;
     uint32_t g = 0;
     Cursor cur = first_cursor(p);
-    const uint8_t* rows[2] = {nullptr, nullptr};
-#define DSV4_LD(DST, ROW, C) DST = rows[ROW] != nullptr ? ldg_stream(rows[ROW] + (C) * 16) : make_uint4(0, 0, 0, 0)
-#define DSV4_LOAD_PAIR(M)                                           \
-  do {                                                              \
-    _Pragma("unroll") for (int h = 0; h < 2; ++h) {                 \
-      if ((M) == 0 || (M) == 2) {                                   \
-        DSV4_LD(ev[h][0], h, 8 * (M) + r);                          \
-        DSV4_LD(ev[h][1], h, 8 * (M) + 4 + r);                      \
-      } else if ((M) == 1) {                                        \
-        DSV4_LD(od[h][0], h, 8 + r);                                \
-        DSV4_LD(od[h][1], h, 12 + r);                               \
-      } else {                                                      \
-        DSV4_LD(od[h][0], h, 24 + r);                               \
-        DSV4_LD(od[h][1], h, 28 + r);                               \
-        DSV4_LD(od[h][2], h, 32 + r);                               \
-      }                                                             \
-    }                                                               \
+#define DSV4_LOAD(I, C)                                                                        \
+  raw[I] = rowp != nullptr ? ldg_stream(rowp + (C) * 16) : make_uint4(0, 0, 0, 0)
+#define DSV4_LOAD_PAIR(M)                      \
+  do {                                         \
+    if ((M) < 3) {                             \
+      DSV4_LOAD(2 * (M), 8 * (M) + r);         \
+      DSV4_LOAD(2 * (M) + 1, 8 * (M) + 4 + r); \
+    } else {                                   \
+      DSV4_LOAD(6, 24 + r);                    \
+      DSV4_LOAD(7, 28 + r);                    \
+      DSV4_LOAD(8, 32 + r);                    \
+    }                                          \
   } while (0)
-#define DSV4_STORE_NOPE(V, J, I)                                                   \
-  do {                                                                             \
-    _Pragma("unroll") for (int h = 0; h < 2; ++h) {                                \
-      uint4 lo, hi;                                                                \
-      dequant16(V[h][J], scale_byte(sc[h], I), lo, hi);                            \
-      st_shared_v4(k_base + (I) * kSubTileBytes + h * kRow64 + off_lo, lo);        \
-      st_shared_v4(k_base + (I) * kSubTileBytes + h * kRow64 + off_hi, hi);        \
-    }                                                                              \
-  } while (0)
-    // Rows and scale bytes of block BLK from its slot table (then released).
-#define DSV4_TAKE(BLK, SC)                                                                   \
-  do {                                                                                       \
-    const int tb_ = (BLK) % kTabBufs;                                                        \
-    ok = ok && mbar_wait(&bars->tab_full[tb_], ((BLK) / kTabBufs) & 1, abort_flag);          \
-    const SlotEntry e0_ = tabs[tb_ * kSlots + s], e1_ = tabs[tb_ * kSlots + s + 64];         \
-    mbar_arrive(&bars->tab_empty[tb_]);                                                      \
-    rows[0] = e0_.row;                                                                       \
-    rows[1] = e1_.row;                                                                       \
-    SC[0] = e0_.scales;                                                                      \
-    SC[1] = e1_.scales;                                                                      \
+#define DSV4_STORE_NOPE(I)                                         \
+  do {                                                             \
+    uint4 lo, hi;                                                  \
+    dequant16(raw[I], scale_byte(sc, I), lo, hi);                  \
+    st_shared_v4(kbuf + (I) * kSubTileBytes + off_lo, lo);         \
+    st_shared_v4(kbuf + (I) * kSubTileBytes + off_hi, hi);         \
   } while (0)
     if (cur.valid) {
-      DSV4_TAKE(0u, sc);
+      ok = mbar_wait(&bars->tab_full[0], 0, abort_flag);
+      const SlotEntry e = tabs[s];
+      mbar_arrive(&bars->tab_empty[0]);
+      const uint8_t* rowp = e.row;
+      sc = e.scales;
       DSV4_LOAD_PAIR(0);
       DSV4_LOAD_PAIR(1);
+      DSV4_LOAD_PAIR(2);
+      DSV4_LOAD_PAIR(3);
     }
+#ifdef CSAHCA_DSV4_TRACE
+    uint32_t p_items = 0;
+#endif
     while (ok && cur.valid) {
+#ifdef CSAHCA_DSV4_TRACE
+      if (pt == 0 && p_items == 0 && cur.blk < 8) DSV4_TRACE(0, cur.blk, 0);
+#endif
       const Cursor nxt = next_cursor(p, cur);
+      const uint8_t* rowp = nullptr;
+      uint2 sc_next = make_uint2(0, 0);
+      if (nxt.valid) {
+        const int tb = (g + 1) % kTabBufs;
+        ok = mbar_wait(&bars->tab_full[tb], ((g + 1) / kTabBufs) & 1, abort_flag);
+        const SlotEntry e = tabs[tb * kSlots + s];
+        mbar_arrive(&bars->tab_empty[tb]);
+        rowp = e.row;
+        sc_next = e.scales;
+      }
+      const int b = g % kKBufs;
+      const uint32_t kbuf = k_base + uint32_t(b) * kBlockBytes;
 #pragma unroll
       for (int m = 0; m < 4; ++m) {
-        if (g >= 1) ok = ok && mbar_wait(&bars->k_empty[0][m], (g - 1) & 1, abort_flag);
-        if (m == 0) {
-          DSV4_STORE_NOPE(ev, 0, 0);
-          DSV4_STORE_NOPE(ev, 1, 1);
-        } else if (m == 1) {
-          DSV4_STORE_NOPE(od, 0, 2);
-          DSV4_STORE_NOPE(od, 1, 3);
-        } else if (m == 2) {
-          DSV4_STORE_NOPE(ev, 0, 4);
-          DSV4_STORE_NOPE(ev, 1, 5);
+        if (g >= kKBufs) ok = ok && mbar_wait(&bars->k_empty[b][m], ((g / kKBufs) - 1) & 1, abort_flag);
+#ifdef CSAHCA_DSV4_TRACE
+        if (pt == 0 && m == 0 && p_items == 0 && cur.blk < 8) DSV4_TRACE(0, cur.blk, 12);
+#endif
+        if (m < 3) {
+          DSV4_STORE_NOPE(2 * m);
+          DSV4_STORE_NOPE(2 * m + 1);
         } else {
-          DSV4_STORE_NOPE(od, 0, 6);
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            st_shared_v4(k_base + h * kRow64 + off_r0, od[h][1]);
-            st_shared_v4(k_base + h * kRow64 + off_r1, od[h][2]);
-          }
+          DSV4_STORE_NOPE(6);
+          st_shared_v4(kbuf + off_r0, raw[7]);
+          st_shared_v4(kbuf + off_r1, raw[8]);
         }
         fence_proxy_async_smem();
-        mbar_arrive(&bars->k_full[0][m]);
-        if (m == 0) {
-          DSV4_LOAD_PAIR(2);
-        } else if (m == 1) {
-          DSV4_LOAD_PAIR(3);
-        } else if (m == 3 && nxt.valid) {
-          // This block is stored; switch to the next block's rows and scales.
-          DSV4_TAKE(g + 1, sc);
-          DSV4_LOAD_PAIR(0);
-          DSV4_LOAD_PAIR(1);
-        }
+        mbar_arrive(&bars->k_full[b][m]);
+        if (nxt.valid) DSV4_LOAD_PAIR(m);
       }
 #undef DSV4_STORE_NOPE
+#ifdef CSAHCA_DSV4_TRACE
+      if (pt == 0 && p_items == 0 && cur.blk < 8) DSV4_TRACE(0, cur.blk, 2);
+      if (cur.blk == cur.nblk - 1) ++p_items;
+#endif
+      sc = sc_next;
       ++g;
       cur = nxt;
     }
-#undef DSV4_TAKE
 #undef DSV4_LOAD_PAIR
-#undef DSV4_LD
+#undef DSV4_LOAD
     if (!ok) failed = true;
   } else if (warp >= kResWarp0 && warp < kResWarp0 + kResWarps) {
     // ------------------------------------------------------------ slot-table resolvers
@@ -627,37 +616,30 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
     // table buffer is free (every producer and softmax thread has read it).
     // The resolvers thus run up to kTabBufs blocks ahead of the producers, and
     // the row prefetches reach L2 long before the producers' register loads.
-    const int rs = threadIdx.x - kResWarp0 * 32;  // slots rs and rs + 64
+    const int rs = threadIdx.x - kResWarp0 * 32;
     bool ok = true;
     uint32_t j = 0;
     Cursor c0 = first_cursor(p);
     Cursor c1 = next_cursor(p, c0);
     Cursor c2 = next_cursor(p, c1);
-    SlotEntry e0[2], e1[2];
-    PendingSlot ps[2];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      e0[h].row = e1[h].row = nullptr;
-      e0[h].scales = e1[h].scales = make_uint2(0, 0);
-      ps[h].loc = -1;
-      ps[h].main = true;
-      if (c0.valid) e0[h] = finish_slot(p, slot_loc(p, c0.sp, c0.blk, rs + 64 * h));
-      if (c1.valid) e1[h] = finish_slot(p, slot_loc(p, c1.sp, c1.blk, rs + 64 * h));
-      if (c2.valid) ps[h] = slot_loc(p, c2.sp, c2.blk, rs + 64 * h);
-    }
+    SlotEntry e0, e1;
+    e0.row = e1.row = nullptr;
+    e0.scales = e1.scales = make_uint2(0, 0);
+    PendingSlot ps;
+    ps.loc = -1;
+    ps.main = true;
+    if (c0.valid) e0 = finish_slot(p, slot_loc(p, c0.sp, c0.blk, rs));
+    if (c1.valid) e1 = finish_slot(p, slot_loc(p, c1.sp, c1.blk, rs));
+    if (c2.valid) ps = slot_loc(p, c2.sp, c2.blk, rs);
     while (c0.valid) {
       const int tb = j % kTabBufs;
       if (j >= kTabBufs && !(ok = mbar_wait(&bars->tab_empty[tb], ((j / kTabBufs) - 1) & 1, abort_flag))) break;
-      tabs[tb * kSlots + rs] = e0[0];
-      tabs[tb * kSlots + rs + 64] = e0[1];
+      tabs[tb * kSlots + rs] = e0;
       mbar_arrive(&bars->tab_full[tb]);
       const Cursor c3 = next_cursor(p, c2);
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        e0[h] = e1[h];
-        if (c2.valid) e1[h] = finish_slot(p, ps[h]);
-        if (c3.valid) ps[h] = slot_loc(p, c3.sp, c3.blk, rs + 64 * h);
-      }
+      e0 = e1;
+      if (c2.valid) e1 = finish_slot(p, ps);
+      if (c3.valid) ps = slot_loc(p, c3.sp, c3.blk, rs);
       c0 = c1;
       c1 = c2;
       c2 = c3;
@@ -700,9 +682,9 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
     // ------------------------------------------------------------ MMA issuer
     // Event-driven issue: PV(g) goes out as soon as the softmax has published
     // P(g); QK(g+1) goes out pair by pair as the producers finish each K pair.
-    // QK(g) may start only once PV(g-kKBufs) is issued (that PV's p_full wait
-    // proves the softmax has finished reading S buffer g%kKBufs).  PV has
-    // priority, since it frees K pairs for the producers.
+    // QK(g) may start only once PV(g-2) is issued (that PV's p_full wait proves
+    // the softmax has finished reading S buffer g%2).  PV has priority, since it
+    // frees K pairs for the producers.
     if (lane == 0) {
       uint32_t gq = 0, gp = 0, q_items = 0, pv_items = 0;
       int mq = 0;            // next K pair of QK(gq)
@@ -743,7 +725,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
             progressed = true;
           }
         }
-        if (!progressed && qk.valid && gq + 1 <= gp + kKBufs) {
+        if (!progressed && qk.valid && gq <= gp + 1) {
           const int bq = gq % kKBufs;
           bool ready = true;
           if (qk.blk == 0 && !q_ready) {
@@ -804,8 +786,8 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
     // only then), and the per-head sums stay per lane in TMEM (columns kTmemL+) until
     // the query ends.
     const int t = threadIdx.x;
-    const bool has_slot = true;  // M = 128: TMEM lane t holds the S^T row of slot t
-    const int slot = t;
+    const bool has_slot = lane < 16;
+    const int slot = 16 * warp + lane;
     const uint32_t t_lane = tmem + (uint32_t(warp * 32) << 16);
     const float sl2 = p.scale_log2;
     constexpr int esz = sizeof(QT);
