@@ -394,6 +394,18 @@ def bench_secondary(dev, hbm: float) -> dict:
     out["csa_cfg1 (config 1: B1 H8 S32768 k8, L2 flushed per step)"] = {
         "us_per_step_dynamic": round(ms * 1e3, 2), "us_decode_precomputed": round(ms_dec * 1e3, 2),
         "decode_gbs_selected_kv": round(8 * 512 * 128 * 2 * 2 / (ms_dec / 1e3) / 1e9, 1)}
+    # the same step with the chunk-sum cache: append this step's K row, select on the sums, decode
+    sums = ext.chunk_sums_build(k, 64)
+    pos = torch.tensor([32767], dtype=torch.int32, device=dev)
+
+    def cached_step():
+        ext.chunk_sums_append(k, sums, pos, 64)
+        sel_c = ext.select_topk_chunks_from_sums(q, sums, 8, chunk_size=64)
+        return ext.csa_decode_forward_tiled(q, k, v, sel_c, 64, 8)
+
+    ms_cached = _time_flushed(cached_step, dev, iters=200)
+    out["csa_cfg1 (config 1: B1 H8 S32768 k8, L2 flushed per step)"]["us_per_step_dynamic_chunk_sum_cache"] = \
+        round(ms_cached * 1e3, 2)
     out["mini_block (config 3: d1024 H8 S32768 c64 k8 mlp 2.0, ms/token, L2 flushed)"] = bench_mini_block(dev)
     return out
 

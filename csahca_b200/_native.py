@@ -40,6 +40,11 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.csahca_csa_select_topk.restype = _int
     lib.csahca_csa_select_topk.argtypes = [_vp, _vp, _vp, _int, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _sz, _vp]
 
+    lib.csahca_csa_chunk_sums_build.restype = _int
+    lib.csahca_csa_chunk_sums_build.argtypes = [_vp, _int, _i64, _i64, _i64, _i64, _i64, _vp, _vp]
+    lib.csahca_csa_chunk_sums_append.restype = _int
+    lib.csahca_csa_chunk_sums_append.argtypes = [_vp, _int, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp]
+
     lib.csahca_csa_decode_workspace_size.restype = _sz
     lib.csahca_csa_decode_workspace_size.argtypes = [_i64, _i64, _i64, _i64, _i64]
     lib.csahca_csa_decode.restype = _int

@@ -147,6 +147,40 @@ def select_topk_chunks(q: torch.Tensor, k_cache: torch.Tensor, chunk_size: int, 
     return out
 
 
+# ------------------------------------------------------------------------------------ chunk-sum cache
+def chunk_sums_build(k_cache: torch.Tensor, chunk_size: int) -> torch.Tensor:
+    """fp32 chunk sums ``[B, H, S // chunk_size, D]`` of ``k_cache`` (the cache
+    that replaces the scorer's full read of K during decoding)."""
+    lib = N.lib()
+    k_cache = k_cache.contiguous()
+    b, h, s, d = k_cache.shape
+    sums = torch.empty((b, h, s // chunk_size, d), dtype=torch.float32, device=k_cache.device)
+    with torch.cuda.device(k_cache.device):
+        N.check(lib.csahca_csa_chunk_sums_build(k_cache.data_ptr(), N.DTYPE_CODE[k_cache.dtype], b, h, s, d,
+                                                int(chunk_size), sums.data_ptr(), N.stream_handle(k_cache.device)))
+    return sums
+
+
+def chunk_sums_append(k_cache: torch.Tensor, sums: torch.Tensor, positions: torch.Tensor, chunk_size: int) -> None:
+    """Fold the K row each request just wrote (``positions``: int32 ``[B]``) into ``sums`` in place."""
+    lib = N.lib()
+    b, h, s, d = k_cache.shape
+    positions = positions.to(device=k_cache.device, dtype=torch.int32).contiguous()
+    with torch.cuda.device(k_cache.device):
+        N.check(lib.csahca_csa_chunk_sums_append(k_cache.data_ptr(), N.DTYPE_CODE[k_cache.dtype], b, h, s, d,
+                                                 int(chunk_size), positions.data_ptr(), sums.data_ptr(),
+                                                 N.stream_handle(k_cache.device)))
+
+
+def select_topk_chunks_from_sums(q: torch.Tensor, sums: torch.Tensor, top_k: int,
+                                 seq_lens: torch.Tensor | None = None, chunk_size: int = 64) -> torch.Tensor:
+    """``select_topk_chunks`` on the chunk-sum cache: same indices (up to fp32
+    rounding of near-equal scores), reading 1/(chunk*dtype-bytes/4) of the bytes.
+    ``seq_lens`` is in tokens, as for ``select_topk_chunks``."""
+    lens = None if seq_lens is None else (seq_lens.to(torch.int32) // int(chunk_size))
+    return select_topk_chunks(q.float(), sums, 1, top_k, lens)
+
+
 def csa_decode_step(q, k_cache, v_cache, chunk_size: int, top_k: int,
                     seq_lens: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
     """One dynamic-selection CSA decode step: ``(output [B,H,D], selected chunks [B,H,k])``."""

@@ -80,6 +80,23 @@ int csahca_csa_select_topk(const void* q, const void* k_cache, const int32_t* se
                            int64_t heads, int64_t seq_len, int64_t head_dim, int64_t chunk_size, int64_t top_k,
                            int32_t* out_indices, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------------ CSA chunk-sum cache
+ * An incremental stand-in for the scorer's read of all of K (the scorer of
+ * hybrid_attention/reference.py:40-56 recomputes every chunk mean each step;
+ * the reference lists caching them as future work).  sums is fp32
+ * [B,H,S/chunk_size,D]: build fills it from k_cache; append adds, for each
+ * request b, the K row at positions[b] (int32 [B]; out-of-range positions are
+ * ignored) into its chunk, the first token of a chunk overwriting.  Selection
+ * on the cache: csahca_csa_select_topk with dtype F32, q converted to fp32,
+ * k_cache = sums, seq_len = S/chunk_size, chunk_size = 1, seq_lens in chunks --
+ * the ranking equals the one on chunk means (a positive constant factor).
+ */
+int csahca_csa_chunk_sums_build(const void* k_cache, int dtype, int64_t batch, int64_t heads, int64_t seq_len,
+                                int64_t head_dim, int64_t chunk_size, float* sums, void* stream);
+int csahca_csa_chunk_sums_append(const void* k_cache, int dtype, int64_t batch, int64_t heads, int64_t seq_len,
+                                 int64_t head_dim, int64_t chunk_size, const int32_t* positions, float* sums,
+                                 void* stream);
+
 /* ------------------------------------------------------------------ CSA decode
  * Split-K decode over the selected chunks with an in-kernel log-sum-exp combine.
  * Replaces csrc/csa_attention.cu:330-385 (csa_decode_forward_cuda) and
