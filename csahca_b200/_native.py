@@ -42,6 +42,9 @@ def _declare(lib: ctypes.CDLL) -> None:
 
     lib.csahca_csa_chunk_sums_build.restype = _int
     lib.csahca_csa_chunk_sums_build.argtypes = [_vp, _int, _i64, _i64, _i64, _i64, _i64, _vp, _vp]
+    lib.csahca_csa_select_topk_from_sums.restype = _int
+    lib.csahca_csa_select_topk_from_sums.argtypes = [_vp, _int, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp,
+                                                     _vp, _sz, _vp]
     lib.csahca_csa_chunk_sums_append.restype = _int
     lib.csahca_csa_chunk_sums_append.argtypes = [_vp, _int, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp]
 

@@ -12,9 +12,16 @@
 //   append: sums[b,h,p/chunk,:] (+)= K[b,h,p,:] for p = positions[b]; the first
 //           token of a chunk (p % chunk == 0) overwrites, so the cache needs no
 //           clearing between requests.
+//   select: one CTA per (b,h) row: warps take chunk rows of the sums (fp32
+//           row-contiguous, 16-byte loads, four rows in flight per warp), dot
+//           them with q into the workspace scores, then the CTA's top-k.  The
+//           cache is a dense [C, D] fp32 matrix per row, so this is a plain
+//           GEMV-plus-select at HBM speed with no per-chunk bookkeeping.
 #include <algorithm>
+#include <cmath>
 
 #include "common.cuh"
+#include "topk.cuh"
 
 namespace csahca {
 namespace {
@@ -78,6 +85,48 @@ int launch_append(const void* k, const int32_t* pos, float* sums, int64_t heads,
   return CSAHCA_OK;
 }
 
+constexpr int kSelSumThreads = 256;
+
+template <typename QT>
+__global__ void __launch_bounds__(kSelSumThreads) select_from_sums_kernel(const QT* q, const float* sums,
+                                                                          const int32_t* seq_lens, int heads,
+                                                                          int nchunks, int dim, int chunk, int kout,
+                                                                          float scale, float* scores, int32_t* out) {
+  __shared__ float s_q[1024];
+  __shared__ unsigned long long s_red[kSelSumThreads / 32];
+  const int row = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int d = threadIdx.x; d < dim; d += kSelSumThreads) s_q[d] = Elem<QT>::to_f(q[size_t(row) * dim + d]);
+  int n = nchunks;
+  if (seq_lens != nullptr) n = min(max(seq_lens[row / heads], 0) / chunk, nchunks);
+  __syncthreads();
+  const float* base = sums + size_t(row) * nchunks * dim;
+  float* sc = scores + size_t(row) * nchunks;
+  constexpr int kRows = 4;
+  for (int c0 = warp * kRows; c0 < n; c0 += (kSelSumThreads / 32) * kRows) {
+    float acc[kRows];
+#pragma unroll
+    for (int i = 0; i < kRows; ++i) acc[i] = 0.f;
+    for (int d = lane * 4; d < dim; d += 128) {
+      float4 v[kRows];
+#pragma unroll
+      for (int i = 0; i < kRows; ++i)
+        v[i] = c0 + i < n ? __ldcs(reinterpret_cast<const float4*>(base + size_t(c0 + i) * dim + d))
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int i = 0; i < kRows; ++i)
+        acc[i] = fmaf(v[i].x, s_q[d], fmaf(v[i].y, s_q[d + 1], fmaf(v[i].z, s_q[d + 2], fmaf(v[i].w, s_q[d + 3], acc[i]))));
+    }
+#pragma unroll
+    for (int i = 0; i < kRows; ++i) {
+      const float t = warp_sum_xor(acc[i], 1, 32);
+      if (lane == 0 && c0 + i < n) sc[c0 + i] = t * scale;
+    }
+  }
+  __syncthreads();
+  topk::block_topk<kSelSumThreads>(sc, n, kout, out + size_t(row) * kout, s_red);
+}
+
 int check_shape(int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim, int64_t chunk) {
   if (chunk <= 0) return csahca_set_arg_error("chunk_size must be positive");
   if (batch < 0 || heads < 0 || seq_len < 0 || head_dim <= 0) return csahca_set_arg_error("sizes must be non-negative");
@@ -121,4 +170,46 @@ extern "C" int csahca_csa_chunk_sums_append(const void* k_cache, int dtype, int6
       return launch_append<float>(k_cache, positions, sums, heads, rows, seq_len, head_dim, chunk_size, st);
     default: return csahca_set_arg_error("unsupported dtype");
   }
+}
+
+extern "C" int csahca_csa_select_topk_from_sums(const void* q, int q_dtype, const float* sums,
+                                                const int32_t* seq_lens, int64_t batch, int64_t heads,
+                                                int64_t num_chunks, int64_t head_dim, int64_t chunk_size,
+                                                int64_t top_k, int32_t* out_indices, void* workspace,
+                                                size_t workspace_bytes, void* stream) {
+  if (int rc = check_shape(batch, heads, num_chunks * chunk_size, head_dim, chunk_size)) return rc;
+  if (top_k <= 0) return csahca_set_arg_error("top_k must be positive");
+  if (head_dim % 4 != 0 || head_dim > 1024) return csahca_set_unsupported("head_dim must be a multiple of 4, <= 1024");
+  if (reinterpret_cast<uintptr_t>(sums) & 15) return csahca_set_arg_error("sums must be 16-byte aligned");
+  const int64_t rows = batch * heads;
+  if (rows == 0 || num_chunks == 0) return CSAHCA_OK;
+  if (workspace_bytes < csahca_csa_select_topk_workspace_size(batch, heads, num_chunks * chunk_size, chunk_size))
+    return csahca_set_arg_error("workspace too small");
+  // Same workspace layout as csahca_csa_select_topk: scores after the ticket and counters.
+  float* scores = reinterpret_cast<float*>(static_cast<char*>(workspace) + 256 + ((size_t(rows) * 4 + 255) & ~size_t(255)));
+  const int kout = int(std::min(top_k, num_chunks));
+  const float scale = float(1.0 / (std::sqrt(double(head_dim)) * double(chunk_size)));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const dim3 grid{static_cast<unsigned>(rows)};
+  switch (q_dtype) {
+    case CSAHCA_DTYPE_BF16:
+      select_from_sums_kernel<__nv_bfloat16><<<grid, kSelSumThreads, 0, st>>>(
+          static_cast<const __nv_bfloat16*>(q), sums, seq_lens, int(heads), int(num_chunks), int(head_dim),
+          int(chunk_size), kout, scale, scores, out_indices);
+      break;
+    case CSAHCA_DTYPE_F16:
+      select_from_sums_kernel<__half><<<grid, kSelSumThreads, 0, st>>>(
+          static_cast<const __half*>(q), sums, seq_lens, int(heads), int(num_chunks), int(head_dim), int(chunk_size),
+          kout, scale, scores, out_indices);
+      break;
+    case CSAHCA_DTYPE_F32:
+      select_from_sums_kernel<float><<<grid, kSelSumThreads, 0, st>>>(
+          static_cast<const float*>(q), sums, seq_lens, int(heads), int(num_chunks), int(head_dim), int(chunk_size),
+          kout, scale, scores, out_indices);
+      break;
+    default:
+      return csahca_set_arg_error("unsupported dtype");
+  }
+  CSAHCA_RETURN_IF_CUDA(cudaGetLastError());
+  return CSAHCA_OK;
 }

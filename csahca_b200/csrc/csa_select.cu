@@ -26,6 +26,7 @@
 
 #include "common.cuh"
 #include "sm100.cuh"
+#include "topk.cuh"
 
 namespace csahca {
 namespace {
@@ -37,7 +38,6 @@ constexpr int kSelWarps = kSelThreads / 32;
 // chunks); small problems shrink the unit so all SMs still get work.
 constexpr int kMaxChunksPerUnit = 64;
 constexpr int kMinChunksPerUnit = 4;
-constexpr int kTopkRegs = 16;  // register path holds up to kSelThreads*kTopkRegs scores
 
 struct SelectParams {
   const void* q;
@@ -102,56 +102,10 @@ __device__ __forceinline__ float chunk_score(const T* rows, int chunk, const flo
   return dot * scale;
 }
 
-__device__ __forceinline__ unsigned long long make_key(float score, int idx) {
-  return (static_cast<unsigned long long>(float_order_key(score)) << 32) | static_cast<unsigned>(~idx);
-}
+using topk::make_key;
 
-// Top-k of scores[0, n) written to out[0, kout): largest first, equal scores by
-// lower index, slots past min(kout, n) get -1.  Called by all threads of a CTA.
-// Round r picks the largest composite key below round r-1's pick, so no element
-// needs to be marked as taken.
-__device__ void block_topk(float* scores, int n, int kout, int32_t* out, unsigned long long* s_red) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const bool in_regs = n <= kSelThreads * kTopkRegs;
-  unsigned long long keys[kTopkRegs];
-  if (in_regs) {
-#pragma unroll
-    for (int e = 0; e < kTopkRegs; ++e) {
-      const int i = tid + e * kSelThreads;
-      keys[e] = i < n ? make_key(__ldcg(scores + i), i) : 0ull;
-    }
-  }
-  const int kvalid = min(kout, n);
-  unsigned long long prev = ~0ull;
-  for (int r = 0; r < kvalid; ++r) {
-    unsigned long long best = 0ull;
-    if (in_regs) {
-#pragma unroll
-      for (int e = 0; e < kTopkRegs; ++e)
-        if (keys[e] < prev && keys[e] > best) best = keys[e];
-    } else {
-      for (int i = tid; i < n; i += kSelThreads) {
-        const unsigned long long kk = make_key(__ldcg(scores + i), i);
-        if (kk < prev && kk > best) best = kk;
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
-      best = other > best ? other : best;
-    }
-    if (lane == 0) s_red[warp] = best;
-    __syncthreads();
-    best = s_red[0];
-#pragma unroll
-    for (int w = 1; w < kSelWarps; ++w) best = s_red[w] > best ? s_red[w] : best;
-    __syncthreads();
-    if (tid == 0) out[r] = static_cast<int32_t>(~static_cast<unsigned>(best & 0xffffffffull));
-    prev = best;
-  }
-  for (int r = kvalid + tid; r < kout; r += kSelThreads) out[r] = -1;
-  __syncthreads();  // leave the workspace zero (see warp_topk)
-  for (int i = tid; i < n; i += kSelThreads) scores[i] = 0.f;
+__device__ __forceinline__ void block_topk(float* scores, int n, int kout, int32_t* out, unsigned long long* s_red) {
+  topk::block_topk<kSelThreads>(scores, n, kout, out, s_red);
 }
 
 template <typename T, int D>

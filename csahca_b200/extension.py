@@ -174,11 +174,28 @@ def chunk_sums_append(k_cache: torch.Tensor, sums: torch.Tensor, positions: torc
 
 def select_topk_chunks_from_sums(q: torch.Tensor, sums: torch.Tensor, top_k: int,
                                  seq_lens: torch.Tensor | None = None, chunk_size: int = 64) -> torch.Tensor:
-    """``select_topk_chunks`` on the chunk-sum cache: same indices (up to fp32
-    rounding of near-equal scores), reading 1/(chunk*dtype-bytes/4) of the bytes.
-    ``seq_lens`` is in tokens, as for ``select_topk_chunks``."""
-    lens = None if seq_lens is None else (seq_lens.to(torch.int32) // int(chunk_size))
-    return select_topk_chunks(q.float(), sums, 1, top_k, lens)
+    """``select_topk_chunks`` on the chunk-sum cache ``[B, H, C, D]`` fp32: the
+    same indices (up to fp32 rounding of near-equal scores) from C*D*4 bytes per
+    row instead of all of K.  ``seq_lens`` is in tokens, as for ``select_topk_chunks``."""
+    if q.ndim != 3 or sums.ndim != 4 or q.shape[:2] != sums.shape[:2] or q.shape[2] != sums.shape[3]:
+        raise ValueError("q must be [B,H,D] and sums [B,H,C,D]")
+    if sums.dtype != torch.float32:
+        raise ValueError("sums must be float32")
+    lib = N.lib()
+    q = q.contiguous()
+    sums = sums.contiguous()
+    b, h, c, d = sums.shape
+    kout = min(int(top_k), c)
+    out = torch.empty((b, h, kout), dtype=torch.int32, device=q.device)
+    if seq_lens is not None:
+        seq_lens = seq_lens.to(device=q.device, dtype=torch.int32).contiguous()
+    with torch.cuda.device(q.device):
+        ws = N.workspaces.get(q.device, lib.csahca_csa_select_topk_workspace_size(b, h, c * chunk_size, chunk_size),
+                              "csa_select")
+        N.check(lib.csahca_csa_select_topk_from_sums(
+            q.data_ptr(), N.DTYPE_CODE[q.dtype], sums.data_ptr(), N.ptr(seq_lens), b, h, c, d, int(chunk_size),
+            int(top_k), out.data_ptr(), ws.data_ptr(), ws.numel(), N.stream_handle(q.device)))
+    return out
 
 
 def csa_decode_step(q, k_cache, v_cache, chunk_size: int, top_k: int,

@@ -86,13 +86,20 @@ int csahca_csa_select_topk(const void* q, const void* k_cache, const int32_t* se
  * the reference lists caching them as future work).  sums is fp32
  * [B,H,S/chunk_size,D]: build fills it from k_cache; append adds, for each
  * request b, the K row at positions[b] (int32 [B]; out-of-range positions are
- * ignored) into its chunk, the first token of a chunk overwriting.  Selection
- * on the cache: csahca_csa_select_topk with dtype F32, q converted to fp32,
- * k_cache = sums, seq_len = S/chunk_size, chunk_size = 1, seq_lens in chunks --
- * the ranking equals the one on chunk means (a positive constant factor).
+ * ignored) into its chunk, the first token of a chunk overwriting.
+ * csahca_csa_select_topk_from_sums selects on the cache exactly as
+ * csahca_csa_select_topk does on k_cache (scores q . sum / chunk / sqrt(D);
+ * same index order, ties and -1 fill; seq_lens in tokens as there; workspace of
+ * csahca_csa_select_topk_workspace_size(B, H, num_chunks * chunk_size,
+ * chunk_size) bytes with the same zero-fill contract).  q of q_dtype, head_dim
+ * a multiple of 4 up to 1024, sums 16-byte aligned.
  */
 int csahca_csa_chunk_sums_build(const void* k_cache, int dtype, int64_t batch, int64_t heads, int64_t seq_len,
                                 int64_t head_dim, int64_t chunk_size, float* sums, void* stream);
+int csahca_csa_select_topk_from_sums(const void* q, int q_dtype, const float* sums, const int32_t* seq_lens,
+                                     int64_t batch, int64_t heads, int64_t num_chunks, int64_t head_dim,
+                                     int64_t chunk_size, int64_t top_k, int32_t* out_indices, void* workspace,
+                                     size_t workspace_bytes, void* stream);
 int csahca_csa_chunk_sums_append(const void* k_cache, int dtype, int64_t batch, int64_t heads, int64_t seq_len,
                                  int64_t head_dim, int64_t chunk_size, const int32_t* positions, float* sums,
                                  void* stream);
