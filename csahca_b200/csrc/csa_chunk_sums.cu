@@ -13,7 +13,7 @@
 //           token of a chunk (p % chunk == 0) overwrites, so the cache needs no
 //           clearing between requests.
 //   select: one CTA per (b,h) row: warps take chunk rows of the sums (fp32
-//           row-contiguous, 16-byte loads, four rows in flight per warp), dot
+//           row-contiguous, 16-byte loads, eight rows in flight per warp), dot
 //           them with q into the workspace scores, then the CTA's top-k.  The
 //           cache is a dense [C, D] fp32 matrix per row, so this is a plain
 //           GEMV-plus-select at HBM speed with no per-chunk bookkeeping.
@@ -85,10 +85,10 @@ int launch_append(const void* k, const int32_t* pos, float* sums, int64_t heads,
   return CSAHCA_OK;
 }
 
-constexpr int kSelSumThreads = 256;
+constexpr int kSelSumThreads = 512;
 
 template <typename QT>
-__global__ void __launch_bounds__(kSelSumThreads) select_from_sums_kernel(const QT* q, const float* sums,
+__global__ void __launch_bounds__(kSelSumThreads, 1) select_from_sums_kernel(const QT* q, const float* sums,
                                                                           const int32_t* seq_lens, int heads,
                                                                           int nchunks, int dim, int chunk, int kout,
                                                                           float scale, float* scores, int32_t* out) {
@@ -102,7 +102,7 @@ __global__ void __launch_bounds__(kSelSumThreads) select_from_sums_kernel(const 
   __syncthreads();
   const float* base = sums + size_t(row) * nchunks * dim;
   float* sc = scores + size_t(row) * nchunks;
-  constexpr int kRows = 4;
+  constexpr int kRows = 8;  // rows in flight per warp: 16 warps x 8 x 512 B per CTA
   for (int c0 = warp * kRows; c0 < n; c0 += (kSelSumThreads / 32) * kRows) {
     float acc[kRows];
 #pragma unroll
