@@ -41,6 +41,23 @@ def test_argument_errors_need_no_gpu():
     assert b"bytes_per_page is too small" in lib.csahca_last_error()
     with pytest.raises(TypeError):
         lib.csahca_csa_select_topk(1, 2, 3)
+    # split-KV entries
+    assert lib.csahca_dsv4_decode_partial(None, 2, 1, 64, None, 1, 37440, 64, None, 8, None, None, 0, 0, 0, None,
+                                          0, None, ctypes.c_float(0.1), 2, 1, 2, None, None, None) == 1
+    assert b"o_partial and lse_partial are required" in lib.csahca_last_error()
+    buf = ctypes.create_string_buffer(64)
+    assert lib.csahca_dsv4_decode_partial(None, 2, 1, 64, None, 1, 37440, 64, None, 8, None, None, 0, 0, 0, None,
+                                          0, None, ctypes.c_float(0.1), 2, 1, 2, buf, buf, None) == 1
+    assert b"invalid shard range" in lib.csahca_last_error()
+    assert lib.csahca_dsv4_combine_partials(None, None, 0, 1, 64, None, None, 2, None) == 1
+    assert b"parts must be in [1, 64]" in lib.csahca_last_error()
+    # chunk-sum cache entries
+    assert lib.csahca_csa_chunk_sums_build(None, 2, 1, 1, 100, 128, 64, None, None) == 1
+    assert b"divisible" in lib.csahca_last_error()
+    assert lib.csahca_csa_chunk_sums_append(None, 2, 1, 1, 128, 128, 64, None, None, None) == 1
+    assert b"positions is required" in lib.csahca_last_error()
+    assert lib.csahca_csa_select_topk_from_sums(None, 2, None, None, 1, 1, 8, 128, 64, 0, None, None, 0, None) == 1
+    assert b"top_k must be positive" in lib.csahca_last_error()
 
 
 def test_workspace_sizes():
