@@ -705,13 +705,18 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
             // O^T[m] += V^T[m] . P^T, V^T read MN-major from the same K tile.
             const uint32_t kbuf = k_base + uint32_t(b) * kBlockBytes;
             const uint32_t pbuf = p_base + uint32_t(b) * kPBytes;
+            // Descriptors are built once; every further MMA only moves the start
+            // address field (bits 0..13, in 16-byte units), which keeps the single
+            // issuing thread at a few instructions per MMA.
+            const uint64_t a_pv = smem_desc_sw128(kbuf, kSubTileBytes, 1024);
+            const uint64_t b_pv = smem_desc_sw128(pbuf, kPBytes, 1024);
+            const uint32_t acc_first = pv.blk != 0;
+#pragma unroll
             for (int m = 0; m < 4; ++m) {
 #pragma unroll
-              for (int kk = 0; kk < kSlots / 16; ++kk) {
-                const uint64_t a = smem_desc_sw128(kbuf + m * kPairBytes + kk * 2048, kSubTileBytes, 1024);
-                const uint64_t bd = smem_desc_sw128(pbuf + kk * 2048, kPBytes, 1024);
-                mma_bf16_ss(tmem + 64 * m, a, bd, kIdescPV, (pv.blk | kk) != 0);
-              }
+              for (int kk = 0; kk < kSlots / 16; ++kk)
+                mma_bf16_ss(tmem + 64 * m, a_pv + uint64_t((m * kPairBytes + kk * 2048) >> 4),
+                            b_pv + uint64_t((kk * 2048) >> 4), kIdescPV, kk == 0 ? acc_first : 1u);
               mma_commit(&bars->k_empty[b][m]);
             }
             mma_commit(&bars->pv_done);
@@ -737,17 +742,16 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
             if (mq == 0) DSV4_TRACE(q_items - 1, qk.blk, 3);
             if (mq == 3) DSV4_TRACE(q_items - 1, qk.blk, 14);
             tc_fence_after();
-            const uint32_t kbufq = k_base + uint32_t(bq) * kBlockBytes;
+            const uint64_t a_qk = smem_desc_sw128(k_base + uint32_t(bq) * kBlockBytes + 2 * mq * kSubTileBytes, 16, 1024);
+            const uint64_t b_qk = smem_desc_sw128(q_base + 2 * mq * (kHeads * 128), 16, 1024);
+            const uint32_t acc_first = mq != 0;
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const int sub = 2 * mq + h;
+            for (int h = 0; h < 2; ++h)
 #pragma unroll
-              for (int kk = 0; kk < 4; ++kk) {
-                const uint64_t a = smem_desc_sw128(kbufq + sub * kSubTileBytes + kk * 32, 16, 1024);
-                const uint64_t bd = smem_desc_sw128(q_base + sub * (kHeads * 128) + kk * 32, 16, 1024);
-                mma_bf16_ss(tmem + kTmemS + 64 * bq, a, bd, kIdescQK, (sub | kk) != 0);
-              }
-            }
+              for (int kk = 0; kk < 4; ++kk)
+                mma_bf16_ss(tmem + kTmemS + 64 * bq, a_qk + uint64_t((h * kSubTileBytes + kk * 32) >> 4),
+                            b_qk + uint64_t((h * kHeads * 128 + kk * 32) >> 4), kIdescQK,
+                            (h | kk) == 0 ? acc_first : 1u);
             if (++mq == 4) {
               mma_commit(&bars->s_full[bq]);
               if (qk.blk == qk.nblk - 1) mma_commit(&bars->q_empty);
