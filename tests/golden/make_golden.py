@@ -1,7 +1,7 @@
 """Generate golden vectors for the oracle from the reference's own PyTorch code.
 
-Run in a container that has the reference checkout (default
-``/root/reference``; override with ``CSAHCA_REFERENCE``):
+Run in a container that has the reference checkout (default: a ``reference``
+directory beside this repository; override with ``CSAHCA_REFERENCE``):
 
     python tests/golden/make_golden.py
 
@@ -22,7 +22,7 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("CSAHCA_REFERENCE", "/root/reference"))
+REF = Path(os.environ.get("CSAHCA_REFERENCE", str(HERE.parents[2].parent / "reference")))
 sys.path.insert(0, str(REF))
 
 from hybrid_attention import dsv4_correctness as D  # noqa: E402
