@@ -22,7 +22,7 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("CSAHCA_REFERENCE", str(HERE.parents[2].parent / "reference")))
+REF = Path(os.environ.get("CSAHCA_REFERENCE", str(HERE.parents[2] / "reference")))
 sys.path.insert(0, str(REF))
 
 from hybrid_attention import dsv4_correctness as D  # noqa: E402
