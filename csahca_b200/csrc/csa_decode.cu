@@ -35,7 +35,7 @@ namespace {
 constexpr int kDecThreads = 256;
 constexpr int kDecWarps = kDecThreads / 32;
 constexpr int kMaxGroup = 16;      // selected chunks per CTA at most
-constexpr int kTargetCtas = 8192;  // split rows until at least this many CTAs
+constexpr int kTargetCtas = 2048;  // split rows until at least this many CTAs (fewer, longer CTAs stream better)
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 

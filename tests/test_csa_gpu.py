@@ -120,7 +120,7 @@ def test_decode_skips_negative_and_out_of_range(cuda, index_dtype):
     assert (out[0, 2] == 0).all()
 
 
-@pytest.mark.parametrize("b,h,top_k", [(1, 2, 32), (1, 1, 3), (16, 32, 16), (64, 32, 16)])
+@pytest.mark.parametrize("b,h,top_k", [(1, 2, 32), (1, 1, 3), (16, 32, 16), (64, 32, 16), (8, 32, 32), (64, 32, 32)])
 def test_split_and_merge_paths(cuda, b, h, top_k):
     """Row splits with the in-kernel last-CTA combine, repeated to exercise the workspace reset."""
     s, d, c = 2048, 128, 64
