@@ -250,6 +250,22 @@ def bench_csa(dev, rank: int, world: int, steps: int, warmup: int, secondary: bo
     torch.cuda.empty_cache()
     if secondary:
         res["secondary"] = bench_secondary(dev, hbm)
+        # The same config-2 step with the chunk-sum cache: fold each
+        # request's newest K row into the cache, select on the cache, decode.
+        sums = ext.chunk_sums_build(k, c)
+        pos = (lens - 1).clamp(min=0)
+
+        def cached_step():
+            ext.chunk_sums_append(k, sums, pos, c)
+            sel_c = ext.select_topk_chunks_from_sums(q, sums, top_k, lens, chunk_size=c)
+            return ext.csa_decode_forward_tiled(q, k, v, sel_c, c)
+
+        ms_c = _time_flushed(cached_step, dev, iters=50)
+        res["secondary"]["csa_cfg2 step with the chunk-sum cache (config 2, same batch)"] = {
+            "us_per_step": round(ms_c * 1e3, 1), "tokens_per_s": round(64 / (ms_c / 1e3), 1),
+            "cache_bytes": sums.numel() * 4,
+            "note": "scorer reads the fp32 chunk sums (1/32 of K) instead of K; not the headline workload"}
+        del sums
     return res
 
 
