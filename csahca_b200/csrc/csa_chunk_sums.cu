@@ -85,10 +85,10 @@ int launch_append(const void* k, const int32_t* pos, float* sums, int64_t heads,
   return CSAHCA_OK;
 }
 
-constexpr int kSelSumThreads = 512;
-
-template <typename QT>
-__global__ void __launch_bounds__(kSelSumThreads, 1) select_from_sums_kernel(const QT* q, const float* sums,
+// Few rows (fewer than SMs): 512 threads per row for more loads in flight;
+// many rows: 256 threads and three CTAs per SM.
+template <typename QT, int kSelSumThreads>
+__global__ void __launch_bounds__(kSelSumThreads, 768 / kSelSumThreads) select_from_sums_kernel(const QT* q, const float* sums,
                                                                           const int32_t* seq_lens, int heads,
                                                                           int nchunks, int dim, int chunk, int kout,
                                                                           float scale, float* scores, int32_t* out) {
@@ -102,7 +102,7 @@ __global__ void __launch_bounds__(kSelSumThreads, 1) select_from_sums_kernel(con
   __syncthreads();
   const float* base = sums + size_t(row) * nchunks * dim;
   float* sc = scores + size_t(row) * nchunks;
-  constexpr int kRows = 8;  // rows in flight per warp: 16 warps x 8 x 512 B per CTA
+  constexpr int kRows = 8;  // chunk rows in flight per warp
   for (int c0 = warp * kRows; c0 < n; c0 += (kSelSumThreads / 32) * kRows) {
     float acc[kRows];
 #pragma unroll
@@ -191,25 +191,25 @@ extern "C" int csahca_csa_select_topk_from_sums(const void* q, int q_dtype, cons
   const float scale = float(1.0 / (std::sqrt(double(head_dim)) * double(chunk_size)));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const dim3 grid{static_cast<unsigned>(rows)};
+  const bool wide = rows < csahca_num_sms();
+#define CSAHCA_SUMS_LAUNCH(QT)                                                                                    \
+  do {                                                                                                           \
+    if (wide)                                                                                                    \
+      select_from_sums_kernel<QT, 512><<<grid, 512, 0, st>>>(static_cast<const QT*>(q), sums, seq_lens, int(heads), \
+                                                              int(num_chunks), int(head_dim), int(chunk_size), kout, \
+                                                              scale, scores, out_indices);                          \
+    else                                                                                                         \
+      select_from_sums_kernel<QT, 256><<<grid, 256, 0, st>>>(static_cast<const QT*>(q), sums, seq_lens, int(heads), \
+                                                              int(num_chunks), int(head_dim), int(chunk_size), kout, \
+                                                              scale, scores, out_indices);                          \
+  } while (0)
   switch (q_dtype) {
-    case CSAHCA_DTYPE_BF16:
-      select_from_sums_kernel<__nv_bfloat16><<<grid, kSelSumThreads, 0, st>>>(
-          static_cast<const __nv_bfloat16*>(q), sums, seq_lens, int(heads), int(num_chunks), int(head_dim),
-          int(chunk_size), kout, scale, scores, out_indices);
-      break;
-    case CSAHCA_DTYPE_F16:
-      select_from_sums_kernel<__half><<<grid, kSelSumThreads, 0, st>>>(
-          static_cast<const __half*>(q), sums, seq_lens, int(heads), int(num_chunks), int(head_dim), int(chunk_size),
-          kout, scale, scores, out_indices);
-      break;
-    case CSAHCA_DTYPE_F32:
-      select_from_sums_kernel<float><<<grid, kSelSumThreads, 0, st>>>(
-          static_cast<const float*>(q), sums, seq_lens, int(heads), int(num_chunks), int(head_dim), int(chunk_size),
-          kout, scale, scores, out_indices);
-      break;
-    default:
-      return csahca_set_arg_error("unsupported dtype");
+    case CSAHCA_DTYPE_BF16: CSAHCA_SUMS_LAUNCH(__nv_bfloat16); break;
+    case CSAHCA_DTYPE_F16: CSAHCA_SUMS_LAUNCH(__half); break;
+    case CSAHCA_DTYPE_F32: CSAHCA_SUMS_LAUNCH(float); break;
+    default: return csahca_set_arg_error("unsupported dtype");
   }
+#undef CSAHCA_SUMS_LAUNCH
   CSAHCA_RETURN_IF_CUDA(cudaGetLastError());
   return CSAHCA_OK;
 }
