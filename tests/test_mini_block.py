@@ -81,3 +81,19 @@ def test_b200_block_selection_and_graph_step(cuda):
         torch.testing.assert_close(out, eager, atol=0, rtol=0)
         out2 = graph.step(out.clone())
         torch.testing.assert_close(out2, blk(eager, k, v, None, **kw), atol=0, rtol=0)
+
+
+def test_block_rejects_the_reference_torch_backends():
+    """The reference's torch-full / torch-csa backends are its oracle and have no
+    counterpart here: asking for them fails before any kernel runs."""
+    from csahca_b200.model_inference import MiniCSADecodeBlock
+
+    blk = MiniCSADecodeBlock(heads=2, head_dim=64, dtype=torch.float32, device=torch.device("cpu"), mlp_ratio=2.0)
+    h = torch.zeros(1, 128)
+    kv = torch.zeros(1, 2, 128, 64)
+    for backend in ("torch-full", "torch-csa"):
+        with pytest.raises(ValueError, match="unknown backend"):
+            blk(h, kv, kv, None, backend=backend, chunk_size=64, top_k=2)
+    with pytest.raises(ValueError, match="unknown variant"):
+        MiniCSADecodeBlock(heads=2, head_dim=64, dtype=torch.float32, device=torch.device("cpu"), mlp_ratio=0.0,
+                           variant="other")
