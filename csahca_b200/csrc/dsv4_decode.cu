@@ -971,15 +971,25 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
             if (t == 0) bulk_wait_read_all();
             named_bar_sync(1, 128);  // the previous round's bulk store has read the staging
           }
+          float o[4][16];
+#pragma unroll
+          for (int m = 0; m < 4; ++m) tmem_ld16(t_lane + 64 * m + h0, o[m]);
+          tmem_wait_ld();
+          if (h0 + per_round >= hcount) {
+            // Every O value has been read: the next query's PV may start now.
+            tc_fence_before();
+            mbar_arrive(&bars->o_empty);
+          }
+          float inv[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) inv[i] = i < per_round ? bars->inv_l[h0 + i] : 0.f;
+#pragma unroll
           for (int m = 0; m < 4; ++m) {
-            float o[16];
-            tmem_ld16(t_lane + 64 * m + h0, o);
-            tmem_wait_ld();
             const int d = 128 * m + t;
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
               if (i < per_round) {
-                const float v = o[i] * bars->inv_l[h0 + i];
+                const float v = o[m][i] * inv[i];
                 const uint32_t a = p_base + uint32_t((i * kDim + d) * oes);
                 if (f32out)
                   asm volatile("st.shared.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
@@ -1001,9 +1011,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
         }
         if (t == 0) bulk_wait_read_all();  // the P buffers are free again for the next query
       }
-      tc_fence_before();
       if (t == 0) DSV4_TRACE(items_done, 0, 11);
-      mbar_arrive(&bars->o_empty);
       named_bar_sync(1, 128);  // inv_l / red consumed before the next query reuses them
       ++items_done;
     }
