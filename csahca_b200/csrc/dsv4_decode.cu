@@ -97,19 +97,9 @@ __device__ long long g_dsv4_trace[2 * 8 * 16];
     if (blockIdx.x == 0 && (item_no) < 2 && (blk) < 8)                                    \
       g_dsv4_trace[((item_no) * 8 + (blk)) * 16 + (ev)] = clock64();                      \
   } while (0)
-// Per producer thread of CTA 0: cycles spent in each producer phase.
-__device__ long long g_dsv4_prod[512 * 4];
-#define DSV4_T0() long long _t0 = clock64()
-#define DSV4_ACC(k) (_acc[k] += clock64() - _t0, _t0 = clock64())
 #else
 #define DSV4_TRACE(item_no, blk, ev) \
   do {                               \
-  } while (0)
-#define DSV4_T0() \
-  do {            \
-  } while (0)
-#define DSV4_ACC(k) \
-  do {              \
   } while (0)
 #endif
 
@@ -1157,11 +1147,6 @@ extern "C" __attribute__((visibility("default"))) int csahca_dsv4_trace_read(lon
   if (n > 2 * 8 * 16) n = 2 * 8 * 16;
   CSAHCA_RETURN_IF_CUDA(cudaDeviceSynchronize());
   CSAHCA_RETURN_IF_CUDA(cudaMemcpyFromSymbol(host, csahca::g_dsv4_trace, sizeof(long long) * n));
-  return CSAHCA_OK;
-}
-extern "C" __attribute__((visibility("default"))) int csahca_dsv4_prod_read(long long* host) {
-  CSAHCA_RETURN_IF_CUDA(cudaDeviceSynchronize());
-  CSAHCA_RETURN_IF_CUDA(cudaMemcpyFromSymbol(host, csahca::g_dsv4_prod, sizeof(long long) * 512 * 4));
   return CSAHCA_OK;
 }
 #endif
