@@ -25,6 +25,7 @@ import torch.distributed as dist
 from . import _native as N
 
 DSV4_HEAD_DIM = 512
+MAX_SHARDS = 64  # csahca_dsv4_combine_partials merges at most this many shards
 
 
 def shard_range(n: int, rank: int, world: int) -> tuple[int, int]:
@@ -127,7 +128,10 @@ def dsv4_split_kv_decode(q, paged_k_cache_u8, token_indices, topk_lengths, extra
     rank = dist.get_rank(group) if distributed else 0
     if local_splits is None:
         local_splits = auto_local_splits(q.shape[0], token_indices.shape[1] // world, q.device)
+        local_splits = min(local_splits, MAX_SHARDS // world)  # the combine merges at most MAX_SHARDS shards
     local_splits = max(1, int(local_splits))
+    if world * local_splits > MAX_SHARDS:
+        raise ValueError(f"at most {MAX_SHARDS} shards in total (world x local_splits)")
     has_extra = (extra_paged_k_cache_u8 is not None and extra_token_indices is not None
                  and extra_token_indices.numel() > 0)
     o, lse = partial_fn(q, paged_k_cache_u8, token_indices, topk_lengths,
