@@ -369,6 +369,8 @@ DSV4_CASES = {
         dict(num_queries=256, heads=64, context=65536, ratio=4, n_main=512, n_extra=64),
     "dsv4_c128 (config 5: Q256 H64 ctx 65536, 512 + 64 C128 slots)":
         dict(num_queries=256, heads=64, context=65536, ratio=128, n_main=512, n_extra=64),
+    "dsv4_c4_q1 (config 5 shape, one query: latency; the slots are split over the SMs)":
+        dict(num_queries=1, heads=64, context=65536, ratio=4, n_main=512, n_extra=64),
 }
 
 

@@ -14,6 +14,8 @@ tune the reference's split, and results do not depend on them.
 
 from __future__ import annotations
 
+import os
+
 import torch
 
 from . import _native as N
@@ -91,14 +93,40 @@ def csa_decode_forward_tiled(q, k_cache, v_cache, chunk_indices, chunk_size: int
 
 
 # ---------------------------------------------------------------------------------------------- DSV4
+def _dsv4_auto_shards(q, token_indices, xidx) -> int:
+    """Shards per query for a DSV4 launch: 1 while the queries alone keep at
+    least half of the SMs busy; otherwise enough 64-slot shards to cover the
+    SMs (at most 64).  ``CSAHCA_DSV4_SPLIT=0`` turns splitting off."""
+    if os.environ.get("CSAHCA_DSV4_SPLIT", "1").strip().lower() in {"0", "false", "no", "off"}:
+        return 1
+    from .split_kv import MAX_SHARDS, _sm_count
+
+    items = q.shape[0] * ((q.shape[1] + 63) // 64)
+    sms = _sm_count(q.device.index if q.device.index is not None else torch.cuda.current_device())
+    if 2 * items > sms:
+        return 1
+    slots = token_indices.shape[1] + (xidx.shape[1] if xidx is not None else 0)
+    return max(1, min(sms // items, slots // 64, MAX_SHARDS))
+
+
 def _launch_dsv4(q, cache, token_indices, topk_lengths, xcache, xidx, xlens, sink, page_size, xpage_size,
                  softmax_scale) -> torch.Tensor:
     lib = N.lib()
-    out = torch.empty_like(q)
     nq, heads, _ = q.shape
     if nq == 0 or heads == 0:
-        return out
+        return torch.empty_like(q)
     has_extra = xcache is not None and xidx is not None and xcache.numel() > 0 and xidx.numel() > 0
+    shards = _dsv4_auto_shards(q, token_indices, xidx if has_extra else None)
+    if shards > 1:
+        # Few queries: split every query's slot lists over several CTAs (the
+        # reference's tiled path splits the same way) and merge the shards.
+        from .split_kv import dsv4_combine_partials, dsv4_decode_partial
+
+        o, lse = dsv4_decode_partial(q, cache, token_indices, topk_lengths, xcache if has_extra else None,
+                                     xidx if has_extra else None, xlens if has_extra else None, page_size,
+                                     xpage_size, softmax_scale, 0, shards, shards)
+        return dsv4_combine_partials(o, lse, sink, q.dtype)
+    out = torch.empty_like(q)
     lens_ptr = topk_lengths.data_ptr() if topk_lengths is not None and topk_lengths.numel() > 0 else None
     sink_ptr = sink.data_ptr() if sink is not None and sink.numel() > 0 else None
     xl_ptr = xlens.data_ptr() if has_extra and xlens is not None and xlens.numel() > 0 else None

@@ -34,10 +34,14 @@ def _t(a, device):
 @pytest.mark.parametrize("name", ["dsv4_c0", "dsv4_c4", "dsv4_c128", "dsv4_c0_f32q"])
 @pytest.mark.parametrize("sink", [True, False])
 @pytest.mark.parametrize("tiled", ["1", "0"])
-def test_golden_cases(cuda, name, sink, tiled, monkeypatch):
+@pytest.mark.parametrize("split", ["1", "0"])
+def test_golden_cases(cuda, name, sink, tiled, split, monkeypatch):
+    """``split``: few queries are split over several CTAs and merged (default)
+    or decoded one CTA per query (CSAHCA_DSV4_SPLIT=0)."""
     if tiled == "0" and not sink:
         pytest.skip("the reference's non-tiled entries reject an absent sink (empty tensor, numel != heads)")
     monkeypatch.setenv("CSAHCA_DSV4_TILED", tiled)
+    monkeypatch.setenv("CSAHCA_DSV4_SPLIT", split)
     z = np.load(GOLDEN / f"{name}.npz")
     dt = str(z["dtype"])
     page = int(z["meta"][4])
@@ -104,7 +108,9 @@ def _check(out, ref, qdtype, rows=None):
 
 
 @pytest.mark.parametrize("heads", [8, 16, 64, 96, 128])
-def test_head_counts(cuda, heads):
+@pytest.mark.parametrize("split", ["1", "0"])
+def test_head_counts(cuda, heads, split, monkeypatch):
+    monkeypatch.setenv("CSAHCA_DSV4_SPLIT", split)
     c = _case(1, 5, heads, 700, 200, 64, neg_frac=0.1)
     _check(_run(c, cuda), _ref(c), "bf16")
 
