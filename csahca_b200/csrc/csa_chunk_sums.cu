@@ -12,15 +12,12 @@
 //   append: sums[b,h,p/chunk,:] (+)= K[b,h,p,:] for p = positions[b]; the first
 //           token of a chunk (p % chunk == 0) overwrites, so the cache needs no
 //           clearing between requests.
-//   select: few rows -> a cluster of CTAs per row (each a range of chunks,
-//           candidates merged through distributed shared memory); otherwise
-//           one CTA per (b,h) row: warps take chunk rows of the sums (fp32
+//   select: one CTA per (b,h) row: warps take chunk rows of the sums (fp32
 //           row-contiguous, 16-byte loads, eight rows in flight per warp), dot
 //           them with q into the workspace scores, then the CTA's top-k.  The
 //           cache is a dense [C, D] fp32 matrix per row, so this is a plain
 //           GEMV-plus-select at HBM speed with no per-chunk bookkeeping.
 #include <algorithm>
-#include <cooperative_groups.h>
 #include <cmath>
 
 #include "common.cuh"
@@ -130,109 +127,6 @@ __global__ void __launch_bounds__(kSelSumThreads, 768 / kSelSumThreads) select_f
   topk::block_topk<kSelSumThreads>(sc, n, kout, out + size_t(row) * kout, s_red);
 }
 
-// Few rows: a row's chunks are spread over a cluster of `CL` CTAs; each scores
-// its range and keeps its top-k as 64-bit keys in shared memory, and rank 0
-// merges the CL x kout candidates through distributed shared memory.  One round
-// of loads per CTA instead of several: the select is latency-bound here.
-constexpr int kClusterThreads = 256;
-constexpr int kMaxClusterK = 64;
-
-template <typename QT>
-__global__ void __launch_bounds__(kClusterThreads) select_from_sums_cluster_kernel(
-    const QT* q, const float* sums, const int32_t* seq_lens, int heads, int nchunks, int dim, int chunk, int kout,
-    float scale, float* scores, int32_t* out) {
-  namespace cg = cooperative_groups;
-  cg::cluster_group cluster = cg::this_cluster();
-  __shared__ float s_q[1024];
-  __shared__ unsigned long long s_red[kClusterThreads / 32];
-  __shared__ unsigned long long s_keys[kMaxClusterK];
-  const int cl = int(cluster.num_blocks());
-  const int rank = int(cluster.block_rank());
-  const int row = blockIdx.x / cl;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  for (int d = tid; d < dim; d += kClusterThreads) s_q[d] = Elem<QT>::to_f(q[size_t(row) * dim + d]);
-  int n = nchunks;
-  if (seq_lens != nullptr) n = min(max(seq_lens[row / heads], 0) / chunk, nchunks);
-  const int lo = int((int64_t(n) * rank) / cl), hi = int((int64_t(n) * (rank + 1)) / cl);
-  __syncthreads();
-  const float* base = sums + size_t(row) * nchunks * dim;
-  float* sc = scores + size_t(row) * nchunks;
-  constexpr int kRows = 8;
-  for (int c0 = lo + warp * kRows; c0 < hi; c0 += (kClusterThreads / 32) * kRows) {
-    float acc[kRows];
-#pragma unroll
-    for (int i = 0; i < kRows; ++i) acc[i] = 0.f;
-    for (int d = lane * 4; d < dim; d += 128) {
-      float4 v[kRows];
-#pragma unroll
-      for (int i = 0; i < kRows; ++i)
-        v[i] = c0 + i < hi ? __ldcs(reinterpret_cast<const float4*>(base + size_t(c0 + i) * dim + d))
-                           : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-      for (int i = 0; i < kRows; ++i)
-        acc[i] = fmaf(v[i].x, s_q[d], fmaf(v[i].y, s_q[d + 1], fmaf(v[i].z, s_q[d + 2], fmaf(v[i].w, s_q[d + 3], acc[i]))));
-    }
-#pragma unroll
-    for (int i = 0; i < kRows; ++i) {
-      const float t = warp_sum_xor(acc[i], 1, 32);
-      if (lane == 0 && c0 + i < hi) sc[c0 + i] = t * scale;
-    }
-  }
-  __syncthreads();
-  // Local top-k over [lo, hi) as keys (largest first; 0 marks "none").
-  unsigned long long prev = ~0ull;
-  for (int r = 0; r < kout; ++r) {
-    unsigned long long best = 0ull;
-    for (int i = lo + tid; i < hi; i += kClusterThreads) {
-      const unsigned long long kk = topk::make_key(__ldcg(sc + i), i);
-      if (kk < prev && kk > best) best = kk;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
-      best = other > best ? other : best;
-    }
-    if (lane == 0) s_red[warp] = best;
-    __syncthreads();
-    best = s_red[0];
-#pragma unroll
-    for (int w = 1; w < kClusterThreads / 32; ++w) best = s_red[w] > best ? s_red[w] : best;
-    __syncthreads();
-    if (tid == 0) s_keys[r] = best;
-    prev = best;
-  }
-  for (int i = lo + tid; i < hi; i += kClusterThreads) sc[i] = 0.f;  // leave the workspace zero
-  cluster.sync();
-  if (rank == 0) {
-    // Merge: each thread takes candidates tid, tid + 256, ... of the CL x kout keys.
-    const int total = cl * kout;
-    unsigned long long prevm = ~0ull;
-    const int kvalid = min(kout, n);
-    for (int r = 0; r < kvalid; ++r) {
-      unsigned long long best = 0ull;
-      for (int i = tid; i < total; i += kClusterThreads) {
-        const unsigned long long kk = cluster.map_shared_rank(s_keys, i / kout)[i % kout];
-        if (kk < prevm && kk > best) best = kk;
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
-        best = other > best ? other : best;
-      }
-      if (lane == 0) s_red[warp] = best;
-      __syncthreads();
-      best = s_red[0];
-#pragma unroll
-      for (int w = 1; w < kClusterThreads / 32; ++w) best = s_red[w] > best ? s_red[w] : best;
-      __syncthreads();
-      if (tid == 0) out[size_t(row) * kout + r] = static_cast<int32_t>(~static_cast<unsigned>(best & 0xffffffffull));
-      prevm = best;
-    }
-    for (int r = kvalid + tid; r < kout; r += kClusterThreads) out[size_t(row) * kout + r] = -1;
-  }
-  cluster.sync();  // peers keep their candidates until rank 0 has read them
-}
-
 int check_shape(int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim, int64_t chunk) {
   if (chunk <= 0) return csahca_set_arg_error("chunk_size must be positive");
   if (batch < 0 || heads < 0 || seq_len < 0 || head_dim <= 0) return csahca_set_arg_error("sizes must be non-negative");
@@ -297,43 +191,7 @@ extern "C" int csahca_csa_select_topk_from_sums(const void* q, int q_dtype, cons
   const float scale = float(1.0 / (std::sqrt(double(head_dim)) * double(chunk_size)));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const dim3 grid{static_cast<unsigned>(rows)};
-  const int sms = csahca_num_sms();
-  const int cl = int(std::min<int64_t>(8, std::min<int64_t>(sms / std::max<int64_t>(rows, 1), num_chunks / 8)));
-  if (kout <= kMaxClusterK && 2 * rows <= sms && cl >= 2) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(rows * cl));
-    cfg.blockDim = dim3(kClusterThreads);
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = unsigned(cl);
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    const int h = int(heads), c = int(num_chunks), dd = int(head_dim), ch = int(chunk_size);
-    switch (q_dtype) {
-      case CSAHCA_DTYPE_BF16:
-        CSAHCA_RETURN_IF_CUDA(cudaLaunchKernelEx(&cfg, select_from_sums_cluster_kernel<__nv_bfloat16>,
-                                                 static_cast<const __nv_bfloat16*>(q), sums, seq_lens, h, c, dd, ch,
-                                                 kout, scale, scores, out_indices));
-        break;
-      case CSAHCA_DTYPE_F16:
-        CSAHCA_RETURN_IF_CUDA(cudaLaunchKernelEx(&cfg, select_from_sums_cluster_kernel<__half>,
-                                                 static_cast<const __half*>(q), sums, seq_lens, h, c, dd, ch, kout,
-                                                 scale, scores, out_indices));
-        break;
-      case CSAHCA_DTYPE_F32:
-        CSAHCA_RETURN_IF_CUDA(cudaLaunchKernelEx(&cfg, select_from_sums_cluster_kernel<float>,
-                                                 static_cast<const float*>(q), sums, seq_lens, h, c, dd, ch, kout,
-                                                 scale, scores, out_indices));
-        break;
-      default:
-        return csahca_set_arg_error("unsupported dtype");
-    }
-    return CSAHCA_OK;
-  }
-  const bool wide = rows < sms;
+  const bool wide = rows < csahca_num_sms();
 #define CSAHCA_SUMS_LAUNCH(QT)                                                                                    \
   do {                                                                                                           \
     if (wide)                                                                                                    \
