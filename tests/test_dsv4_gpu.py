@@ -215,3 +215,17 @@ def test_capturable_in_cuda_graph(cuda):
     g.replay()
     torch.cuda.synchronize()
     assert torch.equal(out, ref)
+
+
+@pytest.mark.parametrize("split", ["1", "0"])
+def test_extra_slots_only_and_empty_main(cuda, split, monkeypatch):
+    """Queries whose main list is empty (length 0 or all -1) but whose compressed
+    list is not, next to queries with both lists empty."""
+    monkeypatch.setenv("CSAHCA_DSV4_SPLIT", split)
+    c = _case(6, 5, 64, 400, 96, 64, xtok=300, nextra=40, xpage=16)
+    c["tl"][:] = [0, 96, 0, 5, 0]
+    c["idx"][2, :] = -1
+    c["xl"][:] = [40, 0, 17, 0, 0]
+    out = _run(c, cuda)
+    _check(out, _ref(c), "bf16")
+    assert (out[4] == 0).all()
