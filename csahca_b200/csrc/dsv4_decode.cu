@@ -343,13 +343,14 @@ __device__ __forceinline__ uint4 load_q8_bf16<float>(const float* src) {
                     *reinterpret_cast<const uint32_t*>(&o2), *reinterpret_cast<const uint32_t*>(&o3));
 }
 
-// Column reduce-scatter over the 32 lanes of a warp: v[64] per lane -> lane L
-// returns the reduction of columns 2L and 2L+1 over all lanes.  Destroys v.
+// Column reduce-scatter within each 16-lane half of a warp: v[32] per lane ->
+// lane L returns the reduction of columns 2(L%16) and 2(L%16)+1 over the 16
+// lanes of its half.  Destroys v.
 template <bool kMax>
-__device__ __forceinline__ float2 warp_colreduce64(float* v) {
+__device__ __forceinline__ float2 halfwarp_colreduce32(float* v) {
   const int lane = threadIdx.x & 31;
 #pragma unroll
-  for (int width = 32, bit = 16; bit >= 1; width >>= 1, bit >>= 1) {
+  for (int width = 16, bit = 8; bit >= 1; width >>= 1, bit >>= 1) {
     const bool upper = (lane & bit) != 0;
 #pragma unroll
     for (int j = 0; j < width; ++j) {
@@ -773,15 +774,18 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
     __syncwarp();
   } else {
     // ------------------------------------------------------------ softmax + epilogue
-    // With M = 64 the S^T row of slot 16w + i (i < 16) sits in TMEM lane 32w + i;
-    // lanes 16..31 of each warp carry no slot and contribute neutral values.
+    // With M = 64 the S^T row of slot 16w + i (i < 16) sits in TMEM lane 32w + i.
+    // The softmax reads it with the half-split shape: lane L of warp w handles
+    // slot 16w + L%16 for the 32 heads 32(L/16) .. 32(L/16)+31, so every lane
+    // of the warp has work.
     // The per-head running max m_use only moves when some score of the block
     // exceeds it by more than 2^8 (block-wide vote; the column-max reduction runs
     // only then), and the per-head sums stay per lane in TMEM (columns kTmemL+) until
     // the query ends.
     const int t = threadIdx.x;
-    const bool has_slot = lane < 16;
-    const int slot = 16 * warp + lane;
+    const int srow = lane & 15, hh = lane >> 4;  // slot row in the warp, head half
+    const int slot = 16 * warp + srow;
+    const int h_lo = 32 * hh;  // first head of this lane's half
     const uint32_t t_lane = tmem + (uint32_t(warp * 32) << 16);
     const float sl2 = p.scale_log2;
     constexpr int esz = sizeof(QT);
@@ -796,14 +800,14 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
       for (int i = t; i < nvec; i += 128) reinterpret_cast<uint4*>(out_q)[i] = make_uint4(0, 0, 0, 0);
       if (p.lse != nullptr && t < hcount) p.lse[size_t(q) * p.heads + hg * kHeads + t] = -INFINITY;
     }
-    // This lane's partial sums of P per head (in the m_use frame) live in TMEM
-    // columns kTmemL .. kTmemL+63 until the query ends.
+    // This lane's partial sums of P over its slot row, per head of its half (in
+    // the m_use frame), live in TMEM columns kTmemL .. kTmemL+63 (first 16 lanes
+    // of the quarter) until the query ends.
     {
       float z[32];
 #pragma unroll
       for (int c = 0; c < 32; ++c) z[c] = 0.f;
-      tmem_st32(t_lane + kTmemL, z);
-      tmem_st32(t_lane + kTmemL + 32, z);
+      tmem_st16x2_32(t_lane + kTmemL, z);
       tmem_wait_st();
     }
     uint32_t g = 0, items_done = 0;
@@ -813,29 +817,25 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
       if (!soft_sync_and(okw)) goto soft_fail;
       if (t == 0) DSV4_TRACE(items_done, cur.blk, 7);
       tc_fence_after();
-      const bool valid = has_slot && tabs[(g % kTabBufs) * kSlots + slot].row != nullptr;
+      const bool valid = tabs[(g % kTabBufs) * kSlots + slot].row != nullptr;
       mbar_arrive(&bars->tab_empty[g % kTabBufs]);
       const uint32_t s_col = kTmemS + 64 * b;
-      float v[32];
+      float v[32];  // S^T of this lane's slot row, heads h_lo .. h_lo+31
       bool over = false;
+      tmem_ld16x2_32(t_lane + s_col, v);
+      tmem_wait_ld();
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        tmem_ld32(t_lane + s_col + 32 * hh, v);
-        tmem_wait_ld();
-#pragma unroll
-        for (int c = 0; c < 32; ++c) over |= fmaf(v[c], sl2, -bars->m_use[32 * hh + c]) > 8.f;
-      }
+      for (int c = 0; c < 32; ++c) over |= fmaf(v[c], sl2, -bars->m_use[h_lo + c]) > 8.f;
       const bool rebase = group_sync_or(1, 128, valid && over);
       if (rebase) {
-        float w64[64];
-        tmem_ld32(t_lane + s_col, w64);
-        tmem_ld32(t_lane + s_col + 32, w64 + 32);
-        tmem_wait_ld();
+        {
+          float w[32];
 #pragma unroll
-        for (int c = 0; c < 64; ++c) w64[c] = valid ? w64[c] * sl2 : -INFINITY;
-        const float2 mx = warp_colreduce64<true>(w64);
-        bars->red[warp][2 * lane] = mx.x;
-        bars->red[warp][2 * lane + 1] = mx.y;
+          for (int c = 0; c < 32; ++c) w[c] = valid ? v[c] * sl2 : -INFINITY;
+          const float2 mx = halfwarp_colreduce32<true>(w);
+          bars->red[warp][h_lo + 2 * srow] = mx.x;
+          bars->red[warp][h_lo + 2 * srow + 1] = mx.y;
+        }
         named_bar_sync(1, 128);
         if (t < kHeads) {
           float bm = bars->red[0][t];
@@ -850,15 +850,15 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
           bars->alpha[t] = alpha;
         }
         named_bar_sync(1, 128);
-#pragma unroll 1
-        for (int hh = 0; hh < 2; ++hh) {
-          tmem_ld32(t_lane + kTmemL + 32 * hh, v);
+        {
+          float la[32];
+          tmem_ld16x2_32(t_lane + kTmemL, la);
           tmem_wait_ld();
 #pragma unroll
-          for (int c = 0; c < 32; ++c) v[c] *= bars->alpha[32 * hh + c];
-          tmem_st32(t_lane + kTmemL + 32 * hh, v);
+          for (int c = 0; c < 32; ++c) la[c] *= bars->alpha[h_lo + c];
+          tmem_st16x2_32(t_lane + kTmemL, la);
+          tmem_wait_st();
         }
-        tmem_wait_st();
         if (cur.blk > 0) {
           // O must hold PV of the previous block before it is re-based.
           const bool okp = mbar_wait(&bars->pv_done, (g - 1) & 1, abort_flag);
@@ -867,12 +867,13 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
 #pragma unroll 1
           for (int m = 0; m < 4; ++m)
 #pragma unroll 1
-            for (int hh = 0; hh < 2; ++hh) {
-              tmem_ld32(t_lane + 64 * m + 32 * hh, v);
+            for (int oh = 0; oh < 2; ++oh) {
+              float o[32];
+              tmem_ld32(t_lane + 64 * m + 32 * oh, o);
               tmem_wait_ld();
 #pragma unroll
-              for (int c = 0; c < 32; ++c) v[c] *= bars->alpha[32 * hh + c];
-              tmem_st32(t_lane + 64 * m + 32 * hh, v);
+              for (int c = 0; c < 32; ++c) o[c] *= bars->alpha[32 * oh + c];
+              tmem_st32(t_lane + 64 * m + 32 * oh, o);
             }
           tmem_wait_st();
         }
@@ -881,11 +882,9 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
       if (t == 0) DSV4_TRACE(items_done, cur.blk, 8);
       // P^T row = 2^(s*scale - m_use) in bf16, swizzled MN-major; sums stay per lane.
       const uint32_t pbuf = p_base + uint32_t(b) * kPBytes;
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
+      {
         float la[32];
-        tmem_ld32(t_lane + s_col + 32 * hh, v);
-        tmem_ld32(t_lane + kTmemL + 32 * hh, la);
+        tmem_ld16x2_32(t_lane + kTmemL, la);
         tmem_wait_ld();
 #pragma unroll
         for (int cc = 0; cc < 4; ++cc) {
@@ -893,16 +892,16 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const int c = 8 * cc + 2 * j;
-            const float p0 = valid ? fast_exp2(fmaf(v[c], sl2, -bars->m_use[32 * hh + c])) : 0.f;
-            const float p1 = valid ? fast_exp2(fmaf(v[c + 1], sl2, -bars->m_use[32 * hh + c + 1])) : 0.f;
+            const float p0 = valid ? fast_exp2(fmaf(v[c], sl2, -bars->m_use[h_lo + c])) : 0.f;
+            const float p1 = valid ? fast_exp2(fmaf(v[c + 1], sl2, -bars->m_use[h_lo + c + 1])) : 0.f;
             la[c] += p0;
             la[c + 1] += p1;
             const __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
             w4[j] = *reinterpret_cast<const uint32_t*>(&b2);
           }
-          if (has_slot) st_shared_v4(pbuf + sw128(slot, 4 * hh + cc), make_uint4(w4[0], w4[1], w4[2], w4[3]));
+          st_shared_v4(pbuf + sw128(slot, 4 * hh + cc), make_uint4(w4[0], w4[1], w4[2], w4[3]));
         }
-        tmem_st32(t_lane + kTmemL + 32 * hh, la);
+        tmem_st16x2_32(t_lane + kTmemL, la);
       }
       tmem_wait_st();
       fence_proxy_async_smem();
@@ -918,17 +917,15 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
       uint8_t* out_q = static_cast<uint8_t*>(p.out) + (size_t(q) * p.heads + size_t(hg) * kHeads) * kDim * oesz;
       {
         // Per-head sums: reduce the lanes' partials once per query.
-        float la[64];
-        tmem_ld32(t_lane + kTmemL, la);
-        tmem_ld32(t_lane + kTmemL + 32, la + 32);
+        float la[32];
+        tmem_ld16x2_32(t_lane + kTmemL, la);
         tmem_wait_ld();
-        const float2 sm = warp_colreduce64<false>(la);
-        bars->red[warp][2 * lane] = sm.x;
-        bars->red[warp][2 * lane + 1] = sm.y;
+        const float2 sm = halfwarp_colreduce32<false>(la);
+        bars->red[warp][h_lo + 2 * srow] = sm.x;
+        bars->red[warp][h_lo + 2 * srow + 1] = sm.y;
 #pragma unroll
         for (int c = 0; c < 32; ++c) la[c] = 0.f;
-        tmem_st32(t_lane + kTmemL, la);
-        tmem_st32(t_lane + kTmemL + 32, la);
+        tmem_st16x2_32(t_lane + kTmemL, la);
         tmem_wait_st();
         const bool okw2 = mbar_wait(&bars->o_full, items_done & 1, abort_flag);
         if (!soft_sync_and(okw2)) goto soft_fail;
