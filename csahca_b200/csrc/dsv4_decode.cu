@@ -702,14 +702,16 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
             const uint64_t a_pv = smem_desc_sw128(kbuf, kSubTileBytes, 1024);
             const uint64_t b_pv = smem_desc_sw128(pbuf, kPBytes, 1024);
             const uint32_t acc_first = pv.blk != 0;
+            // k-step-major order: consecutive MMAs go to the four independent O^T
+            // blocks, so no MMA waits on the accumulation of the one before it.
 #pragma unroll
-            for (int m = 0; m < 4; ++m) {
+            for (int kk = 0; kk < kSlots / 16; ++kk)
 #pragma unroll
-              for (int kk = 0; kk < kSlots / 16; ++kk)
+              for (int m = 0; m < 4; ++m)
                 mma_bf16_ss(tmem + 64 * m, a_pv + uint64_t((m * kPairBytes + kk * 2048) >> 4),
                             b_pv + uint64_t((kk * 2048) >> 4), kIdescPV, kk == 0 ? acc_first : 1u);
-              mma_commit(&bars->k_empty[b][m]);
-            }
+#pragma unroll
+            for (int m = 0; m < 4; ++m) mma_commit(&bars->k_empty[b][m]);
             mma_commit(&bars->pv_done);
             DSV4_TRACE(pv_items, pv.blk, 6);
             if (pv.blk == pv.nblk - 1) {
