@@ -399,6 +399,19 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// log2(x) and 1/x with the hardware approximations (relative error ~2^-22),
+// used once per query for the normalisers.
+__device__ __forceinline__ float fast_log2(float x) {
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float fast_rcp(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // Two adjacent output elements (4 or 8 bytes, aligned) in one store.
 __device__ __forceinline__ void store_pair(__nv_bfloat16* dst, float a, float b) {
   *reinterpret_cast<__nv_bfloat162*>(dst) = __floats2bfloat162_rn(a, b);
@@ -466,6 +479,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   volatile int* abort_flag = &bars->abort_flag;
 
+  if (threadIdx.x == 0) DSV4_TRACE(0, 0, 1);  // kernel entry (exit: item 1, block 0)
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 32);
     mbar_init(&bars->q_empty, 1);
@@ -610,6 +624,20 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
     const int rs = threadIdx.x - kResWarp0 * 32;
     bool ok = true;
     uint32_t j = 0;
+    if (blockIdx.x < p.num_items) {
+      // Pull the first item's index entries into L2 while its lengths load, so
+      // the first slot table waits on one DRAM round trip less.
+      const int qs = blockIdx.x / p.groups;
+      const int q = qs % p.num_queries, sg = p.split0 + qs / p.num_queries;
+      const int lo_m = int((int64_t(p.nmain) * sg) / p.split_total);
+      if (lo_m + rs < p.nmain)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(p.idx + size_t(q) * p.nmain + lo_m + rs) : "memory");
+      if (p.xidx != nullptr && p.nextra > 0) {
+        const int lo_x = int((int64_t(p.nextra) * sg) / p.split_total);
+        if (lo_x + rs < p.nextra)
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(p.xidx + size_t(q) * p.nextra + lo_x + rs) : "memory");
+      }
+    }
     Cursor c0 = first_cursor(p);
     Cursor c1 = next_cursor(p, c0);
     Cursor c2 = next_cursor(p, c1);
@@ -813,11 +841,17 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
       tmem_wait_st();
     }
     uint32_t g = 0, items_done = 0;
+    float sink_l2 = -INFINITY;  // sink logit (log2 units) of head t of the current item, t < kHeads
     for (Cursor cur = first_cursor(p); cur.valid; cur = next_cursor(p, cur), ++g) {
       const int b = g % kKBufs;
       const bool okw = mbar_wait(&bars->s_full[b], (g / kKBufs) & 1, abort_flag);
       if (!soft_sync_and(okw)) goto soft_fail;
       if (t == 0) DSV4_TRACE(items_done, cur.blk, 7);
+      if (cur.blk == 0 && t < kHeads && p.sink != nullptr) {
+        // The sink logit of this thread's head, fetched now so the epilogue does not wait on it.
+        const int hsink = (cur.item % p.groups) * kHeads + t;
+        sink_l2 = hsink < p.heads ? __ldg(p.sink + hsink) * kLog2e : -INFINITY;
+      }
       tc_fence_after();
       const bool valid = tabs[(g % kTabBufs) * kSlots + slot].row != nullptr;
       mbar_arrive(&bars->tab_empty[g % kTabBufs]);
@@ -846,7 +880,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
           const float mo = bars->m_use[t];
           float alpha = 1.f;
           if (bm > mo + 8.f || (mo == -INFINITY && bm != -INFINITY)) {
-            alpha = mo == -INFINITY ? 0.f : exp2f(mo - bm);
+            alpha = mo == -INFINITY ? 0.f : fast_exp2(mo - bm);
             bars->m_use[t] = bm;
           }
           bars->alpha[t] = alpha;
@@ -939,62 +973,71 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
         const float mu = bars->m_use[t];
         if (p.lse != nullptr) {
           if (hg * kHeads + t < p.heads)
-            p.lse[size_t(q) * p.heads + hg * kHeads + t] = (total > 0.f && mu != -INFINITY) ? mu + log2f(total) : -INFINITY;
+            p.lse[size_t(q) * p.heads + hg * kHeads + t] = (total > 0.f && mu != -INFINITY) ? mu + fast_log2(total) : -INFINITY;
         } else if (p.sink != nullptr && hg * kHeads + t < p.heads) {
-          const float sk = p.sink[hg * kHeads + t] * kLog2e;
-          total += (mu == -INFINITY) ? (sk == -INFINITY ? 0.f : INFINITY) : exp2f(sk - mu);
+          total += (mu == -INFINITY) ? (sink_l2 == -INFINITY ? 0.f : INFINITY) : fast_exp2(sink_l2 - mu);
         }
-        bars->inv_l[t] = (total > 0.f && total != INFINITY) ? 1.f / total : 0.f;
+        bars->inv_l[t] = (total > 0.f && total != INFINITY) ? fast_rcp(total) : 0.f;
         bars->m_use[t] = -INFINITY;
       }
       named_bar_sync(1, 128);
       {
         // Stage rounds of heads in the (free) P buffers as [head][512] rows of
         // the output type -- each thread owns one dim of each O^T block -- and
-        // send every round to global memory with one bulk store.
+        // send every round to global memory with one bulk store.  After the
+        // CTA's last block the K buffers are idle (every PV has completed and
+        // the producers are done), so each round gets its own 16 KB there and
+        // no round waits for the previous round's store.
         const bool f32out = p.lse != nullptr || esz == 4;
         const int per_round = f32out ? 8 : 16;  // 16 KB of staging per round
         const int oes = f32out ? 4 : esz;
+        const bool spread = !next_cursor(p, cur).valid;
+        static_assert(kKBufs * kBlockBytes >= 8 * 16384, "K buffers hold every staging round");
+        if (t == 0) DSV4_TRACE(1, 1, 10);
         for (int h0 = 0; h0 < hcount; h0 += per_round) {
-          if (h0 > 0) {
+          if (t == 0) DSV4_TRACE(1, 2 + h0 / per_round, 10);
+          const uint32_t stage = spread ? k_base + uint32_t(h0 / per_round) * 16384u : p_base;
+          if (h0 > 0 && !spread) {
             if (t == 0) bulk_wait_read_all();
             named_bar_sync(1, 128);  // the previous round's bulk store has read the staging
           }
-          float o[4][16];
-#pragma unroll
-          for (int m = 0; m < 4; ++m) tmem_ld16(t_lane + 64 * m + h0, o[m]);
-          tmem_wait_ld();
-          if (h0 + per_round >= hcount) {
-            // Every O value has been read: the next query's PV may start now.
-            tc_fence_before();
-            mbar_arrive(&bars->o_empty);
-          }
+          // One O^T block at a time and no unrolling across blocks: this code runs
+          // once per query, so its size (instruction-cache misses) matters more
+          // than its loop overhead.
           float inv[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) inv[i] = i < per_round ? bars->inv_l[h0 + i] : 0.f;
-#pragma unroll
+#pragma unroll 1
           for (int m = 0; m < 4; ++m) {
-            const int d = 128 * m + t;
+            float o[16];
+            tmem_ld16(t_lane + 64 * m + h0, o);
+            tmem_wait_ld();
+            if (m == 3 && h0 + per_round >= hcount) {
+              // Every O value has been read: the next query's PV may start now.
+              tc_fence_before();
+              mbar_arrive(&bars->o_empty);
+            }
+            const uint32_t a0 = stage + uint32_t((128 * m + t) * oes);
+            if (f32out) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              if (i < per_round) {
-                const float v = o[m][i] * inv[i];
-                const uint32_t a = p_base + uint32_t((i * kDim + d) * oes);
-                if (f32out)
-                  asm volatile("st.shared.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
-                else {
-                  const QT x = Elem<QT>::from_f(v);
-                  asm volatile("st.shared.u16 [%0], %1;" ::"r"(a), "h"(*reinterpret_cast<const unsigned short*>(&x))
-                               : "memory");
-                }
+              for (int i = 0; i < 8; ++i)
+                asm volatile("st.shared.f32 [%0], %1;" ::"r"(a0 + uint32_t(i * kDim * 4)), "f"(o[i] * inv[i]) : "memory");
+            } else {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const QT x = Elem<QT>::from_f(o[i] * inv[i]);
+                asm volatile("st.shared.u16 [%0], %1;" ::"r"(a0 + uint32_t(i * kDim * 2)),
+                             "h"(*reinterpret_cast<const unsigned short*>(&x))
+                             : "memory");
               }
             }
           }
+          if (t == 0) DSV4_TRACE(1, 2 + h0 / per_round, 11);
           fence_proxy_async_smem();
           named_bar_sync(1, 128);
           if (t == 0) {
             const int nh = min(per_round, hcount - h0);
-            bulk_store_s2g(out_q + size_t(h0) * kDim * oes, p_base, uint32_t(nh * kDim * oes));
+            bulk_store_s2g(out_q + size_t(h0) * kDim * oes, stage, uint32_t(nh * kDim * oes));
             bulk_commit();
           }
         }
@@ -1018,6 +1061,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
   tc_fence_before();
   asm volatile("barrier.sync 0;" ::: "memory");
   tc_fence_after();
+  if (threadIdx.x == 0) DSV4_TRACE(1, 0, 1);
   if (warp == kMmaWarp) {
     __syncwarp();
     tmem_dealloc(tmem, kTmemCols);
@@ -1146,6 +1190,11 @@ extern "C" __attribute__((visibility("default"))) int csahca_dsv4_trace_read(lon
   if (n > 2 * 8 * 16) n = 2 * 8 * 16;
   CSAHCA_RETURN_IF_CUDA(cudaDeviceSynchronize());
   CSAHCA_RETURN_IF_CUDA(cudaMemcpyFromSymbol(host, csahca::g_dsv4_trace, sizeof(long long) * n));
+  return CSAHCA_OK;
+}
+extern "C" __attribute__((visibility("default"))) int csahca_dsv4_trace_reset(void) {
+  static long long zeros[2 * 8 * 16] = {};
+  CSAHCA_RETURN_IF_CUDA(cudaMemcpyToSymbol(csahca::g_dsv4_trace, zeros, sizeof(zeros)));
   return CSAHCA_OK;
 }
 #endif
