@@ -700,7 +700,10 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     // Event-driven issue: PV(g) goes out as soon as the softmax has published
-    // P(g); QK(g+1) goes out pair by pair as the producers finish each K pair.
+    // P(g); QK(g+1) goes out pair by pair as the producers finish each K pair,
+    // every consecutive ready pair in one go.  Readiness is polled with the
+    // non-blocking test_wait, so a barrier that is not complete yet never holds
+    // the issuing thread back from another that is.
     // QK(g) may start only once PV(g-2) is issued (that PV's p_full wait proves
     // the softmax has finished reading S buffer g%2).  PV has priority, since it
     // frees K pairs for the producers.
@@ -716,8 +719,8 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
         bool progressed = false;
         if (gp < gq) {
           const int b = gp % kKBufs;
-          bool ready = mbar_try_wait(&bars->p_full[b], (gp / kKBufs) & 1);
-          if (ready && pv.blk == 0 && pv_items > 0) ready = mbar_try_wait(&bars->o_empty, (pv_items - 1) & 1);
+          bool ready = mbar_test_wait(&bars->p_full[b], (gp / kKBufs) & 1);
+          if (ready && pv.blk == 0 && pv_items > 0) ready = mbar_test_wait(&bars->o_empty, (pv_items - 1) & 1);
           if (ready) {
             DSV4_TRACE(pv_items, pv.blk, 5);
             tc_fence_after();
@@ -755,11 +758,11 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
           const int bq = gq % kKBufs;
           bool ready = true;
           if (qk.blk == 0 && !q_ready) {
-            ready = q_ready = mbar_try_wait(&bars->q_full, q_items & 1);
+            ready = q_ready = mbar_test_wait(&bars->q_full, q_items & 1);
             if (q_ready) ++q_items;
           }
-          if (ready) ready = mbar_try_wait(&bars->k_full[bq][mq], (gq / kKBufs) & 1);
-          if (ready) {
+          if (ready) ready = mbar_test_wait(&bars->k_full[bq][mq], (gq / kKBufs) & 1);
+          while (ready) {
             if (mq == 0) DSV4_TRACE(q_items - 1, qk.blk, 3);
             if (mq == 3) DSV4_TRACE(q_items - 1, qk.blk, 14);
             tc_fence_after();
@@ -781,8 +784,11 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
               q_ready = false;
               ++gq;
               qk = next_cursor(p, qk);
+              progressed = true;
+              break;
             }
             progressed = true;
+            ready = mbar_test_wait(&bars->k_full[bq][mq], (gq / kKBufs) & 1);
           }
         }
         if (progressed) {
