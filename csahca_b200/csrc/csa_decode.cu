@@ -81,8 +81,11 @@ __global__ void __launch_bounds__(kDecThreads) csa_decode_kernel(DecodeParams p)
   const int nslots = min(p.group, p.top_k - slot0);
 
   if (tid < nslots) {
+    // A chunk that starts at or past seq_len holds no valid token: mapping it to
+    // -1 here also keeps c * chunk below 2^31 in the token arithmetic below.
     const IdxT c = static_cast<const IdxT*>(p.idx)[size_t(row) * p.top_k + slot0 + tid];
-    s_chunk[tid] = (c < 0 || c > IdxT(0x3fffffff)) ? -1 : int(c);
+    const IdxT nchunks = IdxT((p.seq_len + p.chunk - 1) / p.chunk);
+    s_chunk[tid] = (c < 0 || c >= nchunks) ? -1 : int(c);
   }
   __syncthreads();
 
@@ -421,7 +424,9 @@ extern "C" int csahca_csa_decode(const void* q, const void* k_cache, const void*
 //     the process exits; problems needing more scratch are rejected;
 //   * the first call on a device looks the array's device address up
 //     (cudaGetSymbolAddress) with that device current; make that first call
-//     before any stream capture;
+//     before any stream capture.  The address is kept for the life of the
+//     process, so after cudaDeviceReset (or any reset of the primary context)
+//     the process must be restarted before calling this entry point again;
 //   * all calls share the one array and it keeps the previous call's contents:
 //     each call clears the counters it needs at zero on its own stream, and two
 //     calls whose kernels overlap on the GPU (different streams, or different

@@ -23,6 +23,7 @@ import torch
 import torch.distributed as dist
 
 from . import _native as N
+from .hybrid_attention_cuda import _check, _dsv4_common, _extra_checks
 
 DSV4_HEAD_DIM = 512
 MAX_SHARDS = 64  # csahca_dsv4_combine_partials merges at most this many shards
@@ -70,14 +71,22 @@ def dsv4_decode_partial(q, paged_k_cache_u8, token_indices, topk_lengths, extra_
     """Shards ``shard0 .. shard0+shards-1`` of ``shards_total`` (equal ranges of
     every query's main and extra slot lists, sliced inside the kernel) in one
     launch: ``(o fp32 [shards,Q,H,512], lse fp32 [shards,Q,H])``."""
+    # The same argument checks as the reference-facing entries (device,
+    # contiguity, int32 indices and lengths, page layout): a pointer the kernel
+    # cannot use must fail here, before any launch.
+    _dsv4_common(q, paged_k_cache_u8, token_indices, topk_lengths, None, page_size, tiled=True)
+    x, xi, xl = extra_paged_k_cache_u8, extra_token_indices, extra_topk_lengths
+    has_extra = x is not None and xi is not None and x.numel() > 0 and xi.numel() > 0
+    if has_extra:
+        _extra_checks(x, xi, xl, q.shape[0], extra_page_size, tiled=True)
+    _check(1 <= shards and 0 <= shard0 and shard0 + shards <= shards_total <= MAX_SHARDS,
+           f"shards must satisfy 0 <= shard0 < shard0 + shards <= shards_total <= {MAX_SHARDS}")
     lib = N.lib()
     nq, heads, _ = q.shape
     o = torch.empty((shards, nq, heads, DSV4_HEAD_DIM), dtype=torch.float32, device=q.device)
     lse = torch.empty((shards, nq, heads), dtype=torch.float32, device=q.device)
     if nq == 0 or heads == 0:
         return o, lse
-    x, xi, xl = extra_paged_k_cache_u8, extra_token_indices, extra_topk_lengths
-    has_extra = x is not None and xi is not None and x.numel() > 0 and xi.numel() > 0
     with torch.cuda.device(q.device):
         N.check(lib.csahca_dsv4_decode_partial(
             q.contiguous().data_ptr(), N.DTYPE_CODE[q.dtype], nq, heads,
@@ -95,6 +104,14 @@ def dsv4_decode_partial(q, paged_k_cache_u8, token_indices, topk_lengths, extra_
 def dsv4_combine_partials(o_parts: torch.Tensor, lse_parts: torch.Tensor, attn_sink: torch.Tensor | None,
                           out_dtype: torch.dtype) -> torch.Tensor:
     """Merge ``[G,Q,H,512]`` / ``[G,Q,H]`` shards into ``[Q,H,512]`` of ``out_dtype``."""
+    _check(o_parts.is_cuda and lse_parts.is_cuda, "o_parts and lse_parts must be CUDA tensors")
+    _check(o_parts.dtype == torch.float32 and lse_parts.dtype == torch.float32,
+           "o_parts and lse_parts must be float32")
+    _check(o_parts.dim() == 4 and o_parts.shape[3] == DSV4_HEAD_DIM, "o_parts must be [shards, Q, H, 512]")
+    _check(tuple(lse_parts.shape) == tuple(o_parts.shape[:3]), "lse_parts must be [shards, Q, H]")
+    _check(1 <= o_parts.shape[0] <= MAX_SHARDS, f"between 1 and {MAX_SHARDS} shards")
+    _check(attn_sink is None or attn_sink.numel() in (0, o_parts.shape[2]), "attn_sink must have one value per head")
+    _check(attn_sink is None or attn_sink.device == o_parts.device, "attn_sink must be on the device of o_parts")
     lib = N.lib()
     g, nq, heads, _ = o_parts.shape
     out = torch.empty((nq, heads, DSV4_HEAD_DIM), dtype=out_dtype, device=o_parts.device)

@@ -41,22 +41,44 @@ class CsaBatch:
     seq_lens: torch.Tensor   # [B] int32, multiples of chunk
     chunk: int
     top_k: int
+    request_ids: list[int] | None = None  # which requests of the full batch these rows are
+
+
+def _request_generator(device, seed: int, index: int) -> torch.Generator:
+    g = torch.Generator(device=device)
+    g.manual_seed(seed * 1_000_003 + index + 1)
+    return g
+
+
+def csa_request_lengths(*, batch=64, seq_len=32768, chunk=64, min_len=4096, seed=0) -> list[int]:
+    """Per-request context lengths of the full batch (uniform over multiples of
+    ``chunk`` in [min_len, seq_len]); host-side, so every rank agrees on them."""
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randint(min_len // chunk, seq_len // chunk + 1, (batch,), generator=g) * chunk).tolist()
 
 
 def csa_batched(device, *, batch=64, heads=32, seq_len=32768, head_dim=128, chunk=64, top_k=16,
-                min_len=4096, seed=0, dtype=torch.bfloat16) -> CsaBatch:
-    g = torch.Generator(device=device)
-    g.manual_seed(seed)
-    lens = torch.randint(min_len // chunk, seq_len // chunk + 1, (batch,), generator=g, device=device) * chunk
-    q = torch.randn(batch, heads, head_dim, generator=g, device=device, dtype=dtype)
-    k = torch.empty(batch, heads, seq_len, head_dim, device=device, dtype=dtype)
+                min_len=4096, seed=0, dtype=torch.bfloat16, requests=None) -> CsaBatch:
+    """Config 2's batch, or only the rows ``requests`` of it (a rank's share).
+
+    Every request draws its q, K and V from its own generator, so a request's
+    data is the same whichever subset of the batch is materialised."""
+    lens_all = csa_request_lengths(batch=batch, seq_len=seq_len, chunk=chunk, min_len=min_len, seed=seed)
+    ids = list(range(batch)) if requests is None else [int(r) for r in requests]
+    n = len(ids)
+    q = torch.empty(n, heads, head_dim, device=device, dtype=dtype)
+    k = torch.empty(n, heads, seq_len, head_dim, device=device, dtype=dtype)
     v = torch.empty_like(k)
-    for b in range(batch):  # per request, to bound temporaries
+    for i, r in enumerate(ids):  # per request, to bound temporaries
+        g = _request_generator(device, seed, r)
+        q[i].copy_(torch.randn(heads, head_dim, generator=g, device=device, dtype=dtype))
         kb = torch.randn(heads, seq_len // chunk, chunk, head_dim, generator=g, device=device, dtype=torch.float32)
         kb += torch.randn(heads, seq_len // chunk, 1, 1, generator=g, device=device) * 0.5
-        k[b].copy_(kb.view(heads, seq_len, head_dim))
-        v[b].copy_(torch.randn(heads, seq_len, head_dim, generator=g, device=device, dtype=dtype))
-    return CsaBatch(q, k, v, lens.to(torch.int32), chunk, top_k)
+        k[i].copy_(kb.view(heads, seq_len, head_dim))
+        del kb
+        v[i].copy_(torch.randn(heads, seq_len, head_dim, generator=g, device=device, dtype=dtype))
+    lens = torch.tensor([lens_all[r] for r in ids], dtype=torch.int32, device=device)
+    return CsaBatch(q, k, v, lens, chunk, top_k, ids)
 
 
 def csa_algorithmic_bytes(batch: CsaBatch) -> dict[str, int]:
@@ -117,65 +139,76 @@ class Dsv4Batch:
     extra_topk_lengths: torch.Tensor | None
     attn_sink: torch.Tensor         # [H] fp32
     softmax_scale: float
+    query_ids: list[int] | None = None  # which requests of the full batch these rows are
 
 
 def dsv4_cache(device, *, num_queries=256, heads=64, context=65536, page_size=64, n_main=512, ratio=4,
-               n_extra=64, window=None, seed=0) -> Dsv4Batch:
+               n_extra=64, window=None, seed=0, queries=None) -> Dsv4Batch:
     """Config 5 (ratio 4 / 128, ``n_main`` sampled slots + ``n_extra`` compressed slots)
     or config 4 (ratio 0: the last ``window`` positions of a per-request context in
-    ``context`` = [2048, 16384])."""
-    g = torch.Generator(device=device)
-    g.manual_seed(seed)
-    q = torch.randn(num_queries, heads, HEAD_DIM, generator=g, device=device, dtype=torch.bfloat16)
+    ``context`` = [2048, 16384]).
+
+    ``queries`` selects a subset of the ``num_queries`` requests (a rank's
+    share).  Context lengths and the sink come from one host generator and every
+    request's q, latents and slot choices from its own, so a request decodes to
+    the same output whichever subset is built; only the physical page order
+    (a seeded permutation over the pages built) differs."""
+    master = torch.Generator().manual_seed(seed)
     if ratio == 0:
         lo, hi = context if isinstance(context, tuple) else (context, context)
-        ctx = torch.randint(lo, hi + 1, (num_queries,), generator=g, device=device)
+        ctx_all = torch.randint(lo, hi + 1, (num_queries,), generator=master).tolist()
     else:
-        ctx = torch.full((num_queries,), int(context), device=device)
-    pages_per_req = (ctx + page_size - 1) // page_size
-    total_pages = int(pages_per_req.sum().item())
-    first_page = torch.cumsum(pages_per_req, 0) - pages_per_req
-    perm = torch.randperm(total_pages, generator=g, device=device)
-    cache = torch.zeros(total_pages, bytes_per_page(page_size), dtype=torch.uint8, device=device)
+        ctx_all = [int(context)] * num_queries
+    sink = torch.randn(heads, generator=master, dtype=torch.float32).to(device)
+    ids = list(range(num_queries)) if queries is None else [int(r) for r in queries]
+    nq = len(ids)
+    ctx_host = [ctx_all[r] for r in ids]
+    pages_host = [(L + page_size - 1) // page_size for L in ctx_host]
+    total_pages = sum(pages_host)
+    first_host = [sum(pages_host[:i]) for i in range(nq)]
+    gp = torch.Generator(device=device)
+    gp.manual_seed(seed * 7919 + 17)
+    perm = torch.randperm(max(total_pages, 1), generator=gp, device=device)
+    cache = torch.zeros(max(total_pages, 1), bytes_per_page(page_size), dtype=torch.uint8, device=device)
     xp = 0
     if ratio:
         xp = max(1, page_size // ratio)
         xtok_per_req = int(context) // ratio
         xpages_per_req = (xtok_per_req + xp - 1) // xp
-        xcache = torch.zeros(num_queries * xpages_per_req, bytes_per_page(xp), dtype=torch.uint8, device=device)
-        xperm = torch.randperm(num_queries * xpages_per_req, generator=g, device=device)
-    idx = torch.empty(num_queries, n_main if ratio else (window or 128), dtype=torch.int32, device=device)
-    xidx = torch.empty(num_queries, n_extra, dtype=torch.int32, device=device) if ratio else None
-    ctx_host = ctx.tolist()
-    first_host = first_page.tolist()
-    for r in range(num_queries):
-        L = ctx_host[r]
+        xcache = torch.zeros(max(nq, 1) * xpages_per_req, bytes_per_page(xp), dtype=torch.uint8, device=device)
+        xperm = torch.randperm(max(nq, 1) * xpages_per_req, generator=gp, device=device)
+    q = torch.empty(nq, heads, HEAD_DIM, device=device, dtype=torch.bfloat16)
+    idx = torch.empty(nq, n_main if ratio else (window or 128), dtype=torch.int32, device=device)
+    xidx = torch.empty(nq, n_extra, dtype=torch.int32, device=device) if ratio else None
+    for i, r in enumerate(ids):
+        g = _request_generator(device, seed, r)
+        q[i].copy_(torch.randn(heads, HEAD_DIM, generator=g, device=device, dtype=torch.bfloat16))
+        L = ctx_host[i]
         raw = torch.randn(L, HEAD_DIM, generator=g, device=device, dtype=torch.bfloat16)
         pos = torch.arange(L, device=device)
-        locs = perm[first_host[r] + pos // page_size] * page_size + pos % page_size
+        locs = perm[first_host[i] + pos // page_size] * page_size + pos % page_size
         data, sc = pack_tokens_torch(raw)
         write_rows(cache, page_size, locs, data, sc)
         if ratio:
             sel = torch.randperm(L, generator=g, device=device)[:n_main]
-            idx[r] = locs[sel].to(torch.int32)
+            idx[i] = locs[sel].to(torch.int32)
             comp = raw[: (L // ratio) * ratio].float().view(-1, ratio, HEAD_DIM).mean(1).to(torch.bfloat16)
             xpos = torch.arange(comp.shape[0], device=device)
-            xlocs = xperm[r * xpages_per_req + xpos // xp] * xp + xpos % xp
+            xlocs = xperm[i * xpages_per_req + xpos // xp] * xp + xpos % xp
             xd, xs = pack_tokens_torch(comp)
             write_rows(xcache, xp, xlocs, xd, xs)
             xsel = torch.randperm(comp.shape[0], generator=g, device=device)[:n_extra]
-            xidx[r] = xlocs[xsel].to(torch.int32)
+            xidx[i] = xlocs[xsel].to(torch.int32)
         else:
             w = idx.shape[1]
             lastp = torch.arange(max(0, L - w), L, device=device)
             row = torch.full((w,), -1, dtype=torch.int32, device=device)
             row[: lastp.numel()] = locs[lastp].to(torch.int32)
-            idx[r] = row
-    lens = torch.full((num_queries,), idx.shape[1], dtype=torch.int32, device=device)
-    sink = torch.randn(heads, generator=g, device=device, dtype=torch.float32)
+            idx[i] = row
+    lens = torch.full((nq,), idx.shape[1], dtype=torch.int32, device=device)
     return Dsv4Batch(q, cache, page_size, idx, lens, xcache if ratio else None, xp, xidx,
-                     torch.full((num_queries,), n_extra, dtype=torch.int32, device=device) if ratio else None,
-                     sink, 1.0 / math.sqrt(HEAD_DIM))
+                     torch.full((nq,), n_extra, dtype=torch.int32, device=device) if ratio else None,
+                     sink, 1.0 / math.sqrt(HEAD_DIM), ids)
 
 
 def dsv4_algorithmic_bytes(b: Dsv4Batch) -> int:

@@ -137,7 +137,10 @@ int csahca_csa_decode(const void* q, const void* k_cache, const void* v_cache, c
  * without a device allocator.  Problems whose scratch would exceed
  * csahca_csa_decode_noalloc_max_scratch_bytes() return CSAHCA_EINVAL.  The first
  * call on a device resolves the array's device address; make it before any
- * stream capture.  All calls share the array: calls that overlap on the GPU race.
+ * stream capture.  The address is kept for the life of the process: after
+ * cudaDeviceReset (or any primary-context reset) restart the process before
+ * calling this again.  All calls share the array: calls that overlap on the
+ * GPU race.
  */
 size_t csahca_csa_decode_noalloc_max_scratch_bytes(void);
 int csahca_csa_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, const void* chunk_indices,

@@ -203,3 +203,44 @@ def test_one_gpu_local_splits(cuda, local_splits):
                                d(c["xcache"]), d(c["xidx"]), d(c["xl"]), d(c["sink"]), c["page"], c["xpage"],
                                c["scale"], local_splits=local_splits)
     np.testing.assert_allclose(out.float().cpu().numpy(), to_f32(c["out"], "bf16"), atol=ATOL, rtol=RTOL)
+
+
+def test_partial_and_combine_validate_before_any_launch():
+    """CPU-resident tensors, int64 index lists and mis-shaped partials raise
+    RuntimeError in the Python layer, before the library is touched."""
+    from csahca_b200.split_kv import dsv4_combine_partials, dsv4_decode_partial
+
+    c = _golden()
+    q = torch.from_numpy(c["q"].view(np.int16)).view(torch.bfloat16)
+    cache = torch.from_numpy(c["cache"])
+    idx, tl = torch.from_numpy(c["idx"]), torch.from_numpy(c["tl"])
+    with pytest.raises(RuntimeError, match="q must be CUDA"):
+        dsv4_decode_partial(q, cache, idx, tl, None, None, None, c["page"], 1, c["scale"])
+    with pytest.raises(RuntimeError, match="q must be CUDA"):
+        dsv4_decode_partial(q, cache, idx.to(torch.int64), tl, None, None, None, c["page"], 1, c["scale"])
+    with pytest.raises(RuntimeError, match="must be CUDA tensors"):
+        dsv4_combine_partials(torch.zeros(2, 1, 4, 512), torch.zeros(2, 1, 4), None, torch.bfloat16)
+
+
+@pytest.mark.gpu
+def test_partial_rejects_int64_and_cpu_indices_on_gpu(cuda):
+    from csahca_b200.split_kv import dsv4_combine_partials, dsv4_decode_partial
+
+    c = _golden()
+    q = torch.from_numpy(c["q"].view(np.int16)).view(torch.bfloat16).to(cuda)
+    cache = torch.from_numpy(c["cache"]).to(cuda)
+    idx, tl = torch.from_numpy(c["idx"]).to(cuda), torch.from_numpy(c["tl"]).to(cuda)
+    args = (c["page"], 1, c["scale"])
+    with pytest.raises(RuntimeError, match="token_indices must be int32"):
+        dsv4_decode_partial(q, cache, idx.to(torch.int64), tl, None, None, None, *args)
+    with pytest.raises(RuntimeError, match="token_indices must be CUDA"):
+        dsv4_decode_partial(q, cache, idx.cpu(), tl, None, None, None, *args)
+    with pytest.raises(RuntimeError, match="topk_lengths must be int32"):
+        dsv4_decode_partial(q, cache, idx, tl.to(torch.int64), None, None, None, *args)
+    with pytest.raises(RuntimeError, match="token_indices must be contiguous"):
+        dsv4_decode_partial(q, cache, idx.t().contiguous().t(), tl, None, None, None, *args)
+    with pytest.raises(RuntimeError, match="shards must satisfy"):
+        dsv4_decode_partial(q, cache, idx, tl, None, None, None, *args, shard0=3, shards=2, shards_total=4)
+    o = torch.zeros(2, q.shape[0], q.shape[1], 512, device=cuda)
+    with pytest.raises(RuntimeError, match="lse_parts must be"):
+        dsv4_combine_partials(o, torch.zeros(2, q.shape[0], 3, device=cuda), None, torch.bfloat16)

@@ -33,3 +33,26 @@ def test_csa_batch_shapes_and_bytes():
     assert b.k.shape == (2, 2, 512, 64) and (b.seq_lens % 64 == 0).all() and (b.seq_lens >= 128).all()
     nb = W.csa_algorithmic_bytes(b)
     assert nb["scorer"] >= int(b.seq_lens.sum()) * 2 * 64 * 2
+
+
+def test_request_subsets_reproduce_the_full_batch_rows():
+    """A rank that builds only its share of a batch gets the same rows as the
+    full build (per-request generators), so a sharded run decodes the same job."""
+    kw = dict(batch=5, heads=2, seq_len=256, head_dim=32, chunk=64, top_k=2, min_len=64, seed=3)
+    full = W.csa_batched("cpu", **kw)
+    part = W.csa_batched("cpu", requests=[4, 1], **kw)
+    assert part.request_ids == [4, 1]
+    for i, r in enumerate([4, 1]):
+        assert torch.equal(part.q[i], full.q[r]) and torch.equal(part.k[i], full.k[r])
+        assert torch.equal(part.v[i], full.v[r]) and int(part.seq_lens[i]) == int(full.seq_lens[r])
+    dk = dict(num_queries=4, heads=8, context=256, page_size=16, n_main=32, ratio=4, n_extra=8, seed=2)
+    fd = W.dsv4_cache("cpu", **dk)
+    pd = W.dsv4_cache("cpu", queries=[2, 3], **dk)
+    for i, r in enumerate([2, 3]):
+        assert torch.equal(pd.q[i], fd.q[r])
+        a = dsv4.dequant_dsv4_cache(pd.cache.numpy(), pd.token_indices[i].numpy(), page_size=16)
+        b = dsv4.dequant_dsv4_cache(fd.cache.numpy(), fd.token_indices[r].numpy(), page_size=16)
+        np.testing.assert_array_equal(a, b)
+        a = dsv4.dequant_dsv4_cache(pd.extra_cache.numpy(), pd.extra_token_indices[i].numpy(), page_size=4)
+        b = dsv4.dequant_dsv4_cache(fd.extra_cache.numpy(), fd.extra_token_indices[r].numpy(), page_size=4)
+        np.testing.assert_array_equal(a, b)

@@ -15,6 +15,8 @@ import numpy as np
 import pytest
 import torch
 
+from oracle.numerics import to_f32
+
 pytestmark = pytest.mark.gpu
 ATOL, RTOL = 2e-2, 1e-2  # the bound every other CSA parity test uses
 
@@ -37,23 +39,33 @@ def _call(N, fn, q, k, v, idx, chunk, out):
               N.stream_handle(q.device))
 
 
-@pytest.mark.parametrize("b,h,top_k", [(16, 32, 16), (2, 8, 8)])
+# (16,32,16) and (2,8,8) combine inside a thread-block cluster and touch no
+# scratch.  (1,2,32) splits each row into 32 single-chunk CTAs and (64,32,32)
+# gives 2048 rows x 2 units: both combine through the scratch array (arrival
+# counters + fp32 partials), which is what this entry point exists for.
+@pytest.mark.parametrize("b,h,top_k", [(16, 32, 16), (2, 8, 8), (1, 2, 32), (64, 32, 32)])
 def test_noalloc_matches_workspace_entry_two_calls_in_a_row(cuda, b, h, top_k):
     from csahca_b200 import hybrid_attention_cuda as m
+    from helpers import to_numpy
+    from oracle import csa
 
     N, lib, fn = _entry()
     s, d, c = 2048, 128, 64
-    g = torch.Generator(device=cuda).manual_seed(7 + b)
+    g = torch.Generator(device=cuda).manual_seed(7 + b + top_k)
     q = torch.randn(b, h, d, device=cuda, generator=g).to(torch.bfloat16)
     k = torch.randn(b, h, s, d, device=cuda, generator=g).to(torch.bfloat16)
     v = torch.randn(b, h, s, d, device=cuda, generator=g).to(torch.bfloat16)
     idx = torch.argsort(torch.rand(b, h, s // c, device=cuda, generator=g), dim=-1)[..., :top_k].to(torch.int32)
     ref = m.csa_decode_forward_tiled(q, k, v, idx, c, 8)
+    rows = slice(0, min(b, 2))
+    want = csa.csa_reference(*(to_numpy(t[rows]) for t in (q, k, v)), chunk_size=c, top_k=top_k, dtype="bf16",
+                             selected_chunks=to_numpy(idx[rows]))
     for _ in range(2):
         out = torch.full_like(q, float("nan"))
         assert _call(N, fn, q, k, v, idx, c, out) == 0, lib.csahca_last_error()
         torch.cuda.synchronize()
         np.testing.assert_allclose(out.float().cpu().numpy(), ref.float().cpu().numpy(), atol=ATOL, rtol=RTOL)
+        np.testing.assert_allclose(out[rows].float().cpu().numpy(), to_f32(want, "bf16"), atol=ATOL, rtol=RTOL)
 
 
 def test_noalloc_rejects_problems_beyond_its_scratch(cuda):
