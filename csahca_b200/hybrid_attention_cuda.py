@@ -95,8 +95,9 @@ def csa_decode_forward_tiled(q, k_cache, v_cache, chunk_indices, chunk_size: int
 # ---------------------------------------------------------------------------------------------- DSV4
 def _dsv4_auto_shards(q, token_indices, xidx) -> int:
     """Shards per query for a DSV4 launch: 1 while the queries alone keep at
-    least half of the SMs busy; otherwise enough 64-slot shards to cover the
-    SMs (at most 64).  ``CSAHCA_DSV4_SPLIT=0`` turns splitting off."""
+    least half of the SMs busy or a query has fewer than 256 slots; otherwise
+    enough 64-slot shards to cover the SMs (at most 64).
+    ``CSAHCA_DSV4_SPLIT=0`` turns splitting off."""
     if os.environ.get("CSAHCA_DSV4_SPLIT", "1").strip().lower() in {"0", "false", "no", "off"}:
         return 1
     from .split_kv import MAX_SHARDS, _sm_count
@@ -106,6 +107,11 @@ def _dsv4_auto_shards(q, token_indices, xidx) -> int:
     if 2 * items > sms:
         return 1
     slots = token_indices.shape[1] + (xidx.shape[1] if xidx is not None else 0)
+    if slots < 4 * 64:
+        # Up to three 64-slot blocks per query: a split shortens each CTA's
+        # chain by at most two blocks, less than the merge costs (config 4's
+        # 128-slot window: 23 us unsplit at 128 queries, 39 us split at 64).
+        return 1
     return max(1, min(sms // items, slots // 64, MAX_SHARDS))
 
 

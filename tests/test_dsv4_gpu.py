@@ -111,7 +111,7 @@ def _check(out, ref, qdtype, rows=None):
 @pytest.mark.parametrize("split", ["1", "0"])
 def test_head_counts(cuda, heads, split, monkeypatch):
     monkeypatch.setenv("CSAHCA_DSV4_SPLIT", split)
-    c = _case(1, 5, heads, 700, 200, 64, neg_frac=0.1)
+    c = _case(1, 5, heads, 700, 300, 64, neg_frac=0.1)  # >= 256 slots: the split path is taken
     _check(_run(c, cuda), _ref(c), "bf16")
 
 
