@@ -5,8 +5,11 @@
 //
 // Per query all H heads share one 512-dim latent per slot, with V = K, so the
 // decode is two dense contractions per block of 64 slots:
-//   S^T[slot, head] = K[slot, :] . Q[head, :]          (M=64 slots, N=64 heads, K=512 dims)
+//   S^T[slot, head] = K[slot, :] . Q[head, :]          (K = 512 dims)
 //   O^T[dim,  head] += V^T[dim, slot] . P^T[slot, head]  (M=128 dims x 4, N=64, K=64 slots)
+// The first runs as M=128 x N=128 MMAs that stack the two 256-dim halves of
+// K (rows) and of Q (columns), 16 per block; the diagonal quadrants of the
+// result are the two halves' partial scores, added by the softmax warps.
 // Both run as tcgen05.mma kind::f16 (bf16 operands, fp32 accumulators in TMEM).
 // The dequantised K tile in shared memory is written once in the 128-byte
 // swizzled layout and read as a K-major A operand by the first MMA and as an
@@ -25,10 +28,11 @@
 // Shared memory (1024-byte aligned):
 //   Q      64 heads x 512 dims bf16, 8 K-major sub-tiles of [64 rows x 128 B]     64 KB
 //   K      2 buffers x 8 sub-tiles of [64 slot rows x 128 B]                     128 KB
+//          (sub-tiles in the order 0,4,1,5,2,6,3,7 in both Q and K)
 //   P      2 buffers x 64 slot rows x 64 heads bf16 (MN-major B of the PV MMA)    16 KB
-//   barriers, softmax scratch, slot tables                                       ~6 KB
-// TMEM (512 columns): O^T blocks at columns 0/64/128/192, S^T buffers at 256/320,
-// per-lane P sums at 384.
+//   barriers, softmax scratch, slot tables, score exchange                      ~14 KB
+// TMEM (512 columns): O^T blocks at columns 0/64/128/192, S buffers (128
+// columns each) at 256/384.
 //
 // Slot semantics follow the reference: main slots [0, clamp(topk_lengths[q]))
 // then extra slots [0, clamp(extra_topk_lengths[q])) (dsv4_attention.cu:185-225);
@@ -81,13 +85,16 @@ constexpr uint32_t kOffBar = kOffP + kKBufs * kPBytes;
 constexpr int kTabBufs = 4;                                  // slot tables in flight (see resolvers)
 constexpr uint32_t kBarBytes = 2304;
 constexpr uint32_t kOffTab = kOffBar + kBarBytes;
-constexpr uint32_t kTabBytes = kTabBufs * kSlots * 16;      // 5 KB
-constexpr uint32_t kSmemBytes = kOffTab + kTabBytes + 1024;  // + alignment slack
+constexpr uint32_t kTabBytes = kTabBufs * kSlots * 16;      // 4 KB
+// Score exchange between the two softmax warps of a slot row: 64 slots x 32
+// fp32 partial scores.
+constexpr uint32_t kOffX = kOffTab + kTabBytes;
+constexpr uint32_t kXBytes = kSlots * 32 * 4;                // 8 KB
+constexpr uint32_t kSmemBytes = kOffX + kXBytes + 1024;      // + alignment slack
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemS = 256;  // S^T buffers at columns 256 and 320
-constexpr uint32_t kTmemL = 384;  // per-lane running sums of P per head (64 columns)
+constexpr uint32_t kTmemS = 256;  // S buffers (128 columns each) at columns 256 and 384
 
 // Optional stage timestamps of CTA 0 (build with -DCSAHCA_DSV4_TRACE; diagnosis only).
 #ifdef CSAHCA_DSV4_TRACE
@@ -103,7 +110,16 @@ __device__ long long g_dsv4_trace[2 * 8 * 16];
   } while (0)
 #endif
 
-constexpr uint32_t kIdescQK = idesc_bf16_f32(kSlots, kHeads, 0, 0);
+constexpr uint32_t kIdescQK = idesc_bf16_f32(2 * kSlots, 2 * kHeads, 0, 0);
+
+// K and Q tiles keep their eight 64-dim sub-tiles in the order 0,4,1,5,2,6,3,7,
+// so sub-tiles k and k+4 are adjacent: one M=128 operand holds the same 64
+// slots for dims 64k.. (rows 0-63) and 64(k+4).. (rows 64-127), one N=128
+// operand Q's 64 heads for the same two dim ranges.  The split-K MMA then adds
+// two useful quadrants per instruction (rows 0-63 x columns 0-63 and rows
+// 64-127 x columns 64-127), and every V^T block (dims 128m.., sub-tiles 2m and
+// 2m+1) lies at a fixed 16 KB stride.
+__host__ __device__ constexpr uint32_t sub_pos(int k) { return uint32_t(k < 4 ? 2 * k : 2 * (k - 4) + 1); }
 constexpr uint32_t kIdescPV = idesc_bf16_f32(128, kHeads, 1, 1);
 
 struct Dsv4Params {
@@ -343,24 +359,23 @@ __device__ __forceinline__ uint4 load_q8_bf16<float>(const float* src) {
                     *reinterpret_cast<const uint32_t*>(&o2), *reinterpret_cast<const uint32_t*>(&o3));
 }
 
-// Column reduce-scatter within each 16-lane half of a warp: v[32] per lane ->
-// lane L returns the reduction of columns 2(L%16) and 2(L%16)+1 over the 16
-// lanes of its half.  Destroys v.
+// Column reduce-scatter over a full warp: v[32] per lane -> lane L returns the
+// max (or sum) of column L over the 32 lanes.  Destroys v.
 template <bool kMax>
-__device__ __forceinline__ float2 halfwarp_colreduce32(float* v) {
+__device__ __forceinline__ float warp_colreduce32(float* v) {
   const int lane = threadIdx.x & 31;
 #pragma unroll
-  for (int width = 16, bit = 8; bit >= 1; width >>= 1, bit >>= 1) {
-    const bool upper = (lane & bit) != 0;
+  for (int width = 16; width >= 1; width >>= 1) {
+    const bool upper = (lane & width) != 0;
 #pragma unroll
     for (int j = 0; j < width; ++j) {
       const float send = upper ? v[j] : v[j + width];
       const float keep = upper ? v[j + width] : v[j];
-      const float recv = __shfl_xor_sync(0xffffffffu, send, bit);
+      const float recv = __shfl_xor_sync(0xffffffffu, send, width);
       v[j] = kMax ? fmaxf(keep, recv) : keep + recv;
     }
   }
-  return make_float2(v[0], v[1]);
+  return v[0];
 }
 
 // Named barrier `id` over `n` threads that also ANDs a predicate across them, so
@@ -516,17 +531,19 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
     // 64i + 16r .. +15, scale group i, K sub-tile i), chunks 28..35 are the
     // bf16 rope dims (K sub-tile 7).  The shared-memory offsets are therefore
     // fixed per thread, and four threads read 64 contiguous bytes of a row.
-    // Block g goes to K buffer g%2.  One register set rotates pair by pair:
-    // right after the stores of pair m of block g, the loads of pair m of block
-    // g+1 go out into the same registers, so every row load has a block period
-    // to land.  Invalid slots load nothing and store zeros.
+    // Sub-tile k is stored at position sub_pos(k) of the tile.  Block g goes to
+    // K buffer g%2, in four groups m = {sub-tiles m, m+4} (the operands of one
+    // QK group).  One register set rotates group by group: right after the
+    // stores of group m of block g, the loads of group m of block g+1 go out
+    // into the same registers, so every row load has a block period to land.
+    // Invalid slots load nothing and store zeros.
     const int pt = threadIdx.x - kProdWarp0 * 32;
     const int s = pt >> 2, r = pt & 3;
     const uint32_t x7 = uint32_t(s & 7), row_off = uint32_t(s) * 128u;
     const uint32_t off_lo = row_off + ((uint32_t(2 * r) ^ x7) << 4);
     const uint32_t off_hi = row_off + ((uint32_t(2 * r + 1) ^ x7) << 4);
-    const uint32_t off_r0 = 7u * kSubTileBytes + row_off + ((uint32_t(r) ^ x7) << 4);
-    const uint32_t off_r1 = 7u * kSubTileBytes + row_off + ((uint32_t(r + 4) ^ x7) << 4);
+    const uint32_t off_r0 = sub_pos(7) * kSubTileBytes + row_off + ((uint32_t(r) ^ x7) << 4);
+    const uint32_t off_r1 = sub_pos(7) * kSubTileBytes + row_off + ((uint32_t(r + 4) ^ x7) << 4);
     uint4 raw[9];
     uint2 sc = make_uint2(0, 0);
     bool ok = true;
@@ -537,10 +554,10 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
 #define DSV4_LOAD_PAIR(M)                      \
   do {                                         \
     if ((M) < 3) {                             \
-      DSV4_LOAD(2 * (M), 8 * (M) + r);         \
-      DSV4_LOAD(2 * (M) + 1, 8 * (M) + 4 + r); \
+      DSV4_LOAD((M), 4 * (M) + r);             \
+      DSV4_LOAD((M) + 4, 4 * (M) + 16 + r);    \
     } else {                                   \
-      DSV4_LOAD(6, 24 + r);                    \
+      DSV4_LOAD(3, 12 + r);                    \
       DSV4_LOAD(7, 28 + r);                    \
       DSV4_LOAD(8, 32 + r);                    \
     }                                          \
@@ -549,8 +566,8 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
   do {                                                             \
     uint4 lo, hi;                                                  \
     dequant16(raw[I], scale_byte(sc, I), lo, hi);                  \
-    st_shared_v4(kbuf + (I) * kSubTileBytes + off_lo, lo);         \
-    st_shared_v4(kbuf + (I) * kSubTileBytes + off_hi, hi);         \
+    st_shared_v4(kbuf + sub_pos(I) * kSubTileBytes + off_lo, lo);  \
+    st_shared_v4(kbuf + sub_pos(I) * kSubTileBytes + off_hi, hi);  \
   } while (0)
     if (cur.valid) {
       ok = mbar_wait(&bars->tab_full[0], 0, abort_flag);
@@ -590,10 +607,10 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
         if (pt == 0 && m == 0 && p_items == 0 && cur.blk < 8) DSV4_TRACE(0, cur.blk, 12);
 #endif
         if (m < 3) {
-          DSV4_STORE_NOPE(2 * m);
-          DSV4_STORE_NOPE(2 * m + 1);
+          DSV4_STORE_NOPE(m);
+          DSV4_STORE_NOPE(m + 4);
         } else {
-          DSV4_STORE_NOPE(6);
+          DSV4_STORE_NOPE(3);
           st_shared_v4(kbuf + off_r0, raw[7]);
           st_shared_v4(kbuf + off_r1, raw[8]);
         }
@@ -647,9 +664,19 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
     PendingSlot ps;
     ps.loc = -1;
     ps.main = true;
-    if (c0.valid) e0 = finish_slot(p, slot_loc(p, c0.sp, c0.blk, rs));
-    if (c1.valid) e1 = finish_slot(p, slot_loc(p, c1.sp, c1.blk, rs));
-    if (c2.valid) ps = slot_loc(p, c2.sp, c2.blk, rs);
+    {
+      // The index loads of the first three blocks go out together, then the
+      // scale loads of the first two: two round trips to the first table
+      // instead of five.
+      PendingSlot p0, p1;
+      p0.loc = p1.loc = -1;
+      p0.main = p1.main = true;
+      if (c0.valid) p0 = slot_loc(p, c0.sp, c0.blk, rs);
+      if (c1.valid) p1 = slot_loc(p, c1.sp, c1.blk, rs);
+      if (c2.valid) ps = slot_loc(p, c2.sp, c2.blk, rs);
+      if (c0.valid) e0 = finish_slot(p, p0);
+      if (c1.valid) e1 = finish_slot(p, p1);
+    }
     while (c0.valid) {
       const int tb = j % kTabBufs;
       if (j >= kTabBufs && !(ok = mbar_wait(&bars->tab_empty[tb], ((j / kTabBufs) - 1) & 1, abort_flag))) break;
@@ -682,7 +709,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
       for (int i = lane; i < kHeads * 64; i += 32) {
         const int row = i >> 6, c = i & 63;
         const int head = hg * kHeads + row;
-        const uint32_t dst = q_base + uint32_t(c >> 3) * (kHeads * 128) + sw128(row, c & 7);
+        const uint32_t dst = q_base + sub_pos(c >> 3) * (kHeads * 128) + sw128(row, c & 7);
         if (head >= p.heads) {
           st_shared_v4(dst, make_uint4(0, 0, 0, 0));
         } else if constexpr (std::is_same<QT, __nv_bfloat16>::value) {
@@ -730,19 +757,28 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
             // Descriptors are built once; every further MMA only moves the start
             // address field (bits 0..13, in 16-byte units), which keeps the single
             // issuing thread at a few instructions per MMA.
-            const uint64_t a_pv = smem_desc_sw128(kbuf, kSubTileBytes, 1024);
+            // V^T block m (dims 128m..): sub-tiles 2m and 2m+1, two positions apart.
+            const uint64_t a_pv = smem_desc_sw128(kbuf, 2 * kSubTileBytes, 1024);
             const uint64_t b_pv = smem_desc_sw128(pbuf, kPBytes, 1024);
             const uint32_t acc_first = pv.blk != 0;
-            // k-step-major order: consecutive MMAs go to the four independent O^T
-            // blocks, so no MMA waits on the accumulation of the one before it.
+            // V^T blocks 0 and 2 first (sub-tiles 0,1,4,5: K groups 0 and 1, which
+            // the producers may refill as soon as these MMAs complete), then
+            // blocks 1 and 3 (groups 2 and 3).  Within each half the two blocks
+            // alternate k-step by k-step, so no MMA waits on the accumulation
+            // of the one before it.
 #pragma unroll
-            for (int kk = 0; kk < kSlots / 16; ++kk)
+            for (int half = 0; half < 2; ++half) {
 #pragma unroll
-              for (int m = 0; m < 4; ++m)
-                mma_bf16_ss(tmem + 64 * m, a_pv + uint64_t((m * kPairBytes + kk * 2048) >> 4),
-                            b_pv + uint64_t((kk * 2048) >> 4), kIdescPV, kk == 0 ? acc_first : 1u);
+              for (int kk = 0; kk < kSlots / 16; ++kk)
 #pragma unroll
-            for (int m = 0; m < 4; ++m) mma_commit(&bars->k_empty[b][m]);
+                for (int mm = 0; mm < 2; ++mm) {
+                  const int m = half + 2 * mm;
+                  mma_bf16_ss(tmem + 64 * m, a_pv + uint64_t((sub_pos(2 * m) * kSubTileBytes + kk * 2048) >> 4),
+                              b_pv + uint64_t((kk * 2048) >> 4), kIdescPV, kk == 0 ? acc_first : 1u);
+                }
+              mma_commit(&bars->k_empty[b][2 * half]);
+              mma_commit(&bars->k_empty[b][2 * half + 1]);
+            }
             mma_commit(&bars->pv_done);
             DSV4_TRACE(pv_items, pv.blk, 6);
             if (pv.blk == pv.nblk - 1) {
@@ -769,13 +805,11 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
             const uint64_t a_qk = smem_desc_sw128(k_base + uint32_t(bq) * kBlockBytes + 2 * mq * kSubTileBytes, 16, 1024);
             const uint64_t b_qk = smem_desc_sw128(q_base + 2 * mq * (kHeads * 128), 16, 1024);
             const uint32_t acc_first = mq != 0;
+            // Group mq: sub-tiles mq and mq+4 of K (rows) and Q (columns) at once.
 #pragma unroll
-            for (int h = 0; h < 2; ++h)
-#pragma unroll
-              for (int kk = 0; kk < 4; ++kk)
-                mma_bf16_ss(tmem + kTmemS + 64 * bq, a_qk + uint64_t((h * kSubTileBytes + kk * 32) >> 4),
-                            b_qk + uint64_t((h * kHeads * 128 + kk * 32) >> 4), kIdescQK,
-                            (h | kk) == 0 ? acc_first : 1u);
+            for (int kk = 0; kk < 4; ++kk)
+              mma_bf16_ss(tmem + kTmemS + 128 * bq, a_qk + uint64_t((kk * 32) >> 4), b_qk + uint64_t((kk * 32) >> 4),
+                          kIdescQK, kk == 0 ? acc_first : 1u);
             if (++mq == 4) {
               mma_commit(&bars->s_full[bq]);
               if (qk.blk == qk.nblk - 1) mma_commit(&bars->q_empty);
@@ -810,19 +844,24 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
     __syncwarp();
   } else {
     // ------------------------------------------------------------ softmax + epilogue
-    // With M = 64 the S^T row of slot 16w + i (i < 16) sits in TMEM lane 32w + i.
-    // The softmax reads it with the half-split shape: lane L of warp w handles
-    // slot 16w + L%16 for the 32 heads 32(L/16) .. 32(L/16)+31, so every lane
-    // of the warp has work.
+    // S buffer b (128 columns) holds, for slot s, the partial scores over dims
+    // of sub-tiles 0-3 in lane s, columns 0-63 (heads) and those over sub-tiles
+    // 4-7 in lane 64 + s, columns 64-127.  Warps 0/2 take slots 0-31, warps 1/3
+    // slots 32-63; warps 0-1 own heads 0-31, warps 2-3 heads 32-63.  Each
+    // thread hands the partials of the other half of the heads to its partner
+    // (same slot, other warp pair) through shared memory and adds the
+    // partner's to its own, then works on 32 heads of one slot.
     // The per-head running max m_use only moves when some score of the block
     // exceeds it by more than 2^8 (block-wide vote; the column-max reduction runs
-    // only then), and the per-head sums stay per lane in TMEM (columns kTmemL+) until
-    // the query ends.
+    // only then); each thread keeps its slot's partial sums of P per head in
+    // registers until the query ends.
     const int t = threadIdx.x;
-    const int srow = lane & 15, hh = lane >> 4;  // slot row in the warp, head half
-    const int slot = 16 * warp + srow;
-    const int h_lo = 32 * hh;  // first head of this lane's half
+    const int hh = warp >> 1;                 // head half owned by this thread
+    const int slot = 32 * (warp & 1) + lane;  // slot row of this thread
+    const int h_lo = 32 * hh;                 // first head of this thread's half
     const uint32_t t_lane = tmem + (uint32_t(warp * 32) << 16);
+    const uint32_t x_row = smem_u32(smem + kOffX) + uint32_t(slot) * 128u;
+    const uint32_t x_sw = uint32_t(slot & 7);
     const float sl2 = p.scale_log2;
     constexpr int esz = sizeof(QT);
     // Items without any valid slot: zeros (the sink alone gives a zero output).
@@ -836,16 +875,9 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
       for (int i = t; i < nvec; i += 128) reinterpret_cast<uint4*>(out_q)[i] = make_uint4(0, 0, 0, 0);
       if (p.lse != nullptr && t < hcount) p.lse[size_t(q) * p.heads + hg * kHeads + t] = -INFINITY;
     }
-    // This lane's partial sums of P over its slot row, per head of its half (in
-    // the m_use frame), live in TMEM columns kTmemL .. kTmemL+63 (first 16 lanes
-    // of the quarter) until the query ends.
-    {
-      float z[32];
+    float la[32];  // this slot's partial sums of P per head of this half (m_use frame)
 #pragma unroll
-      for (int c = 0; c < 32; ++c) z[c] = 0.f;
-      tmem_st16x2_32(t_lane + kTmemL, z);
-      tmem_wait_st();
-    }
+    for (int c = 0; c < 32; ++c) la[c] = 0.f;
     uint32_t g = 0, items_done = 0;
     float sink_l2 = -INFINITY;  // sink logit (log2 units) of head t of the current item, t < kHeads
     for (Cursor cur = first_cursor(p); cur.valid; cur = next_cursor(p, cur), ++g) {
@@ -861,11 +893,42 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
       tc_fence_after();
       const bool valid = tabs[(g % kTabBufs) * kSlots + slot].row != nullptr;
       mbar_arrive(&bars->tab_empty[g % kTabBufs]);
-      const uint32_t s_col = kTmemS + 64 * b;
-      float v[32];  // S^T of this lane's slot row, heads h_lo .. h_lo+31
+      const uint32_t s_col = kTmemS + 128 * b;
+      float v[32];  // scores of this thread's slot, heads h_lo .. h_lo+31
+      {
+        float w[32];  // the partner's heads, from this thread's dims
+        tmem_ld32(t_lane + s_col + (hh ? 96 : 0), v);
+        tmem_ld32(t_lane + s_col + (hh ? 64 : 32), w);
+        tmem_wait_ld();
+        // Heads 32-63 of dims 0-255 go from warps 0-1 to warps 2-3, then heads
+        // 0-31 of dims 256-511 back, through one 8 KB buffer.
+#pragma unroll
+        for (int round = 0; round < 2; ++round) {
+          if (hh == round) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              st_shared_v4(x_row + ((uint32_t(j) ^ x_sw) << 4),
+                           make_uint4(__float_as_uint(w[4 * j]), __float_as_uint(w[4 * j + 1]),
+                                      __float_as_uint(w[4 * j + 2]), __float_as_uint(w[4 * j + 3])));
+          }
+          named_bar_sync(1, 128);
+          if (hh != round) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              uint4 x4;
+              asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                           : "=r"(x4.x), "=r"(x4.y), "=r"(x4.z), "=r"(x4.w)
+                           : "r"(x_row + ((uint32_t(j) ^ x_sw) << 4)));
+              v[4 * j] += __uint_as_float(x4.x);
+              v[4 * j + 1] += __uint_as_float(x4.y);
+              v[4 * j + 2] += __uint_as_float(x4.z);
+              v[4 * j + 3] += __uint_as_float(x4.w);
+            }
+          }
+          if (round == 0) named_bar_sync(1, 128);  // the buffer is read before round 1 writes it
+        }
+      }
       bool over = false;
-      tmem_ld16x2_32(t_lane + s_col, v);
-      tmem_wait_ld();
 #pragma unroll
       for (int c = 0; c < 32; ++c) over |= fmaf(v[c], sl2, -bars->m_use[h_lo + c]) > 8.f;
       const bool rebase = group_sync_or(1, 128, valid && over);
@@ -874,15 +937,12 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
           float w[32];
 #pragma unroll
           for (int c = 0; c < 32; ++c) w[c] = valid ? v[c] * sl2 : -INFINITY;
-          const float2 mx = halfwarp_colreduce32<true>(w);
-          bars->red[warp][h_lo + 2 * srow] = mx.x;
-          bars->red[warp][h_lo + 2 * srow + 1] = mx.y;
+          bars->red[warp][lane] = warp_colreduce32<true>(w);  // head h_lo + lane over this warp's 32 slots
         }
         named_bar_sync(1, 128);
         if (t < kHeads) {
-          float bm = bars->red[0][t];
-#pragma unroll
-          for (int w = 1; w < kSoftWarps; ++w) bm = fmaxf(bm, bars->red[w][t]);
+          const int w0 = 2 * (t >> 5);
+          const float bm = fmaxf(bars->red[w0][t & 31], bars->red[w0 + 1][t & 31]);
           const float mo = bars->m_use[t];
           float alpha = 1.f;
           if (bm > mo + 8.f || (mo == -INFINITY && bm != -INFINITY)) {
@@ -892,15 +952,8 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
           bars->alpha[t] = alpha;
         }
         named_bar_sync(1, 128);
-        {
-          float la[32];
-          tmem_ld16x2_32(t_lane + kTmemL, la);
-          tmem_wait_ld();
 #pragma unroll
-          for (int c = 0; c < 32; ++c) la[c] *= bars->alpha[h_lo + c];
-          tmem_st16x2_32(t_lane + kTmemL, la);
-          tmem_wait_st();
-        }
+        for (int c = 0; c < 32; ++c) la[c] *= bars->alpha[h_lo + c];
         if (cur.blk > 0) {
           // O must hold PV of the previous block before it is re-based.
           const bool okp = mbar_wait(&bars->pv_done, (g - 1) & 1, abort_flag);
@@ -922,30 +975,23 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
         named_bar_sync(1, 128);  // alpha consumed before the next re-base writes it
       }
       if (t == 0) DSV4_TRACE(items_done, cur.blk, 8);
-      // P^T row = 2^(s*scale - m_use) in bf16, swizzled MN-major; sums stay per lane.
+      // P^T row = 2^(s*scale - m_use) in bf16, swizzled MN-major; sums in registers.
       const uint32_t pbuf = p_base + uint32_t(b) * kPBytes;
-      {
-        float la[32];
-        tmem_ld16x2_32(t_lane + kTmemL, la);
-        tmem_wait_ld();
 #pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          uint32_t w4[4];
+      for (int cc = 0; cc < 4; ++cc) {
+        uint32_t w4[4];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int c = 8 * cc + 2 * j;
-            const float p0 = valid ? fast_exp2(fmaf(v[c], sl2, -bars->m_use[h_lo + c])) : 0.f;
-            const float p1 = valid ? fast_exp2(fmaf(v[c + 1], sl2, -bars->m_use[h_lo + c + 1])) : 0.f;
-            la[c] += p0;
-            la[c + 1] += p1;
-            const __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
-            w4[j] = *reinterpret_cast<const uint32_t*>(&b2);
-          }
-          st_shared_v4(pbuf + sw128(slot, 4 * hh + cc), make_uint4(w4[0], w4[1], w4[2], w4[3]));
+        for (int j = 0; j < 4; ++j) {
+          const int c = 8 * cc + 2 * j;
+          const float p0 = valid ? fast_exp2(fmaf(v[c], sl2, -bars->m_use[h_lo + c])) : 0.f;
+          const float p1 = valid ? fast_exp2(fmaf(v[c + 1], sl2, -bars->m_use[h_lo + c + 1])) : 0.f;
+          la[c] += p0;
+          la[c + 1] += p1;
+          const __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
+          w4[j] = *reinterpret_cast<const uint32_t*>(&b2);
         }
-        tmem_st16x2_32(t_lane + kTmemL, la);
+        st_shared_v4(pbuf + sw128(slot, 4 * hh + cc), make_uint4(w4[0], w4[1], w4[2], w4[3]));
       }
-      tmem_wait_st();
       fence_proxy_async_smem();
       tc_fence_before();
       if (t == 0) DSV4_TRACE(items_done, cur.blk, 9);
@@ -958,24 +1004,22 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
       const int oesz = p.lse != nullptr ? 4 : esz;
       uint8_t* out_q = static_cast<uint8_t*>(p.out) + (size_t(q) * p.heads + size_t(hg) * kHeads) * kDim * oesz;
       {
-        // Per-head sums: reduce the lanes' partials once per query.
-        float la[32];
-        tmem_ld16x2_32(t_lane + kTmemL, la);
-        tmem_wait_ld();
-        const float2 sm = halfwarp_colreduce32<false>(la);
-        bars->red[warp][h_lo + 2 * srow] = sm.x;
-        bars->red[warp][h_lo + 2 * srow + 1] = sm.y;
+        // Per-head sums: reduce the slots' partials once per query.
+        float tmp[32];
 #pragma unroll
-        for (int c = 0; c < 32; ++c) la[c] = 0.f;
-        tmem_st16x2_32(t_lane + kTmemL, la);
-        tmem_wait_st();
+        for (int c = 0; c < 32; ++c) {
+          tmp[c] = la[c];
+          la[c] = 0.f;
+        }
+        bars->red[warp][lane] = warp_colreduce32<false>(tmp);
         const bool okw2 = mbar_wait(&bars->o_full, items_done & 1, abort_flag);
         if (!soft_sync_and(okw2)) goto soft_fail;
       }
       if (t == 0) DSV4_TRACE(items_done, 0, 10);
       tc_fence_after();
       if (t < kHeads) {
-        float total = bars->red[0][t] + bars->red[1][t] + bars->red[2][t] + bars->red[3][t];
+        const int w0 = 2 * (t >> 5);
+        float total = bars->red[w0][t & 31] + bars->red[w0 + 1][t & 31];
         const float mu = bars->m_use[t];
         if (p.lse != nullptr) {
           if (hg * kHeads + t < p.heads)
