@@ -382,10 +382,11 @@ def _time_flushed(fn, dev, iters=50, warm=5) -> float:
         fn()
     evs = []
     for _ in range(iters):
-        # Keep the GPU busy while the host enqueues the next call, so host-side
-        # launch overhead of short calls does not leak into the events.
-        torch.cuda._sleep(100_000)
+        # L2 flush first, then keep the GPU busy (~0.5 ms spin) while the host
+        # enqueues the events and the call, so host-side overhead of short
+        # calls (argument checks, ctypes) does not leak into the events.
         buf.fill_(1)
+        torch.cuda._sleep(1_000_000)
         a, b = _event(), _event()
         a.record()
         fn()
