@@ -194,16 +194,18 @@ __device__ __forceinline__ SlotSpace slot_space(const Dsv4Params& p, int qs) {
   return s;
 }
 
-// One resolved slot of a block: its 576-byte row (nullptr = skipped) and its 8 scale bytes.
+// One resolved slot of a block: its 576-byte row (nullptr = skipped) and the
+// address of its 8 scale bytes.  The producers load the scale bytes together
+// with the row, so a table costs the resolvers no dependent load.
 struct SlotEntry {
   const uint8_t* row;
-  uint2 scales;
+  const uint2* scales;
 };
 static_assert(sizeof(SlotEntry) == 16, "slot table entry is 16 bytes");
 
 // Slot resolution in two steps for the resolver pipeline: slot_loc() issues the
-// index load, finish_slot() turns the index into the row address and issues
-// the scale-byte load; the caller stores the entry one step later.
+// index load, finish_slot() turns the index into the row and scale addresses
+// (and prefetches the row into L2); the caller stores the entry one step later.
 struct PendingSlot {
   int loc;
   bool main;
@@ -226,7 +228,7 @@ __device__ __forceinline__ PendingSlot slot_loc(const Dsv4Params& p, const SlotS
 __device__ __forceinline__ SlotEntry finish_slot(const Dsv4Params& p, const PendingSlot& ps) {
   SlotEntry e;
   e.row = nullptr;
-  e.scales = make_uint2(0, 0);
+  e.scales = nullptr;
   const int64_t cap = ps.main ? p.capacity : p.xcapacity;
   if (ps.loc >= 0 && ps.loc < cap) {
     const unsigned page_size = unsigned(ps.main ? p.page : p.xpage);
@@ -234,7 +236,7 @@ __device__ __forceinline__ SlotEntry finish_slot(const Dsv4Params& p, const Pend
     const unsigned in_page = unsigned(ps.loc) - page * page_size;
     const uint8_t* pb = (ps.main ? p.cache : p.xcache) + int64_t(page) * (ps.main ? p.bpp : p.xbpp);
     e.row = pb + int64_t(in_page) * kRowBytes;
-    e.scales = __ldg(reinterpret_cast<const uint2*>(pb + int64_t(page_size) * kRowBytes + int64_t(in_page) * kScaleBytes));
+    e.scales = reinterpret_cast<const uint2*>(pb + int64_t(page_size) * kRowBytes + int64_t(in_page) * kScaleBytes);
     // Pull the row into L2 now (two blocks ahead of its register loads): the
     // gather is latency-bound, and this keeps many rows in flight without
     // registers or shared memory.
@@ -574,7 +576,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
       const SlotEntry e = tabs[s];
       mbar_arrive(&bars->tab_empty[0]);
       const uint8_t* rowp = e.row;
-      sc = e.scales;
+      sc = e.row != nullptr ? __ldg(e.scales) : make_uint2(0, 0);
       DSV4_LOAD_PAIR(0);
       DSV4_LOAD_PAIR(1);
       DSV4_LOAD_PAIR(2);
@@ -596,7 +598,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
         const SlotEntry e = tabs[tb * kSlots + s];
         mbar_arrive(&bars->tab_empty[tb]);
         rowp = e.row;
-        sc_next = e.scales;
+        sc_next = e.row != nullptr ? __ldg(e.scales) : make_uint2(0, 0);
       }
       const int b = g % kKBufs;
       const uint32_t kbuf = k_base + uint32_t(b) * kBlockBytes;
@@ -660,7 +662,7 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
     Cursor c2 = next_cursor(p, c1);
     SlotEntry e0, e1;
     e0.row = e1.row = nullptr;
-    e0.scales = e1.scales = make_uint2(0, 0);
+    e0.scales = e1.scales = nullptr;
     PendingSlot ps;
     ps.loc = -1;
     ps.main = true;
