@@ -643,14 +643,18 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
     const int rs = threadIdx.x - kResWarp0 * 32;
     bool ok = true;
     uint32_t j = 0;
+    // The first item's first main index is loaded before its lengths are known
+    // (the load does not depend on them), and its extra indices are pulled into
+    // L2, so the first slot table waits on one DRAM round trip less.
+    int spec_loc = -1, spec_off = -1;
     if (blockIdx.x < p.num_items) {
-      // Pull the first item's index entries into L2 while its lengths load, so
-      // the first slot table waits on one DRAM round trip less.
       const int qs = blockIdx.x / p.groups;
       const int q = qs % p.num_queries, sg = p.split0 + qs / p.num_queries;
       const int lo_m = int((int64_t(p.nmain) * sg) / p.split_total);
-      if (lo_m + rs < p.nmain)
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(p.idx + size_t(q) * p.nmain + lo_m + rs) : "memory");
+      if (lo_m + rs < p.nmain) {
+        spec_off = lo_m;
+        spec_loc = __ldg(p.idx + size_t(q) * p.nmain + lo_m + rs);
+      }
       if (p.xidx != nullptr && p.nextra > 0) {
         const int lo_x = int((int64_t(p.nextra) * sg) / p.split_total);
         if (lo_x + rs < p.nextra)
@@ -673,7 +677,12 @@ __global__ void __launch_bounds__(kThreads, 1) dsv4_decode_kernel(Dsv4Params p) 
       PendingSlot p0, p1;
       p0.loc = p1.loc = -1;
       p0.main = p1.main = true;
-      if (c0.valid) p0 = slot_loc(p, c0.sp, c0.blk, rs);
+      if (c0.valid && c0.item == int(blockIdx.x) && c0.blk == 0 && c0.sp.main_off == spec_off &&
+          rs < c0.sp.len_main) {
+        p0.loc = spec_loc;  // the speculative load above is this slot's index
+      } else if (c0.valid) {
+        p0 = slot_loc(p, c0.sp, c0.blk, rs);
+      }
       if (c1.valid) p1 = slot_loc(p, c1.sp, c1.blk, rs);
       if (c2.valid) ps = slot_loc(p, c2.sp, c2.blk, rs);
       if (c0.valid) e0 = finish_slot(p, p0);
