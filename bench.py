@@ -505,10 +505,39 @@ def bench_dsv4_case(dev, hbm: float, kw: dict, iters: int = 50, warm: int = 5, c
     return res
 
 
+def bench_indexer(dev, hbm: float, nq: int = 256, n: int = 16384, top_k: int = 64) -> dict:
+    """DSV4 compressed-slot indexer at config 5's shape: 256 queries, the 16384
+    C4 slots of a 65536 context, 64 indexer heads of dim 128, top-64."""
+    from csahca_b200 import extension as ext
+    from oracle import indexer
+
+    g = torch.Generator(device=dev).manual_seed(5)
+    q = torch.randn(nq, 64, 128, generator=g, device=dev).to(torch.bfloat16)
+    w = torch.randn(nq, 64, generator=g, device=dev) * 0.1
+    keys = torch.randn(nq, n, 128, generator=g, device=dev, dtype=torch.bfloat16)
+    ms = _time_flushed(lambda: ext.dsv4_indexer_topk(q, w, keys, top_k), dev, iters=30)
+    nb = keys.numel() * 2 + q.numel() * 2 + w.numel() * 4 + nq * top_k * 4
+    flops = 2 * nq * n * 64 * 128
+    s = 2  # CPU sample: queries
+    qh, wh, kh = _host(q[:s]), w[:s].cpu().numpy(), _host(keys[:s])
+    t = _median_time(lambda: indexer.indexer_topk(qh, wh, kh, top_k))
+    res = {"us_per_step": round(ms * 1e3, 2), "tokens_per_s": round(nq / (ms / 1e3), 1),
+           "achieved_gbs": round(nb / (ms / 1e3) / 1e9, 1), "hbm_frac": round(nb / (ms / 1e3) / 1e9 / hbm, 4),
+           "tensor_tflops": round(flops / (ms / 1e3) / 1e12, 1), "algorithmic_bytes": nb,
+           "cpu_baseline": {"value": round(s / t, 2), "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                            "cpu": _cpu_model(), "sample": f"{s} queries (numpy restatement of the published "
+                                                          "indexer score + top-k), median of 3, scaled linearly"}}
+    del q, w, keys
+    torch.cuda.empty_cache()
+    return res
+
+
 def bench_secondary(dev, hbm: float) -> dict:
     from csahca_b200 import extension as ext
 
     out = {}
+    out["dsv4_indexer (config 5 shape: Q256, 16384 C4 slots, 64 x 128 indexer heads, top-64)"] = \
+        bench_indexer(dev, hbm)
     for name, kw in DSV4_CASES.items():
         out[name] = bench_dsv4_case(dev, hbm, kw, cpu="q1" not in name)
     # config 1: B1 H8 S32768 D128 c64 k8, one dynamic step

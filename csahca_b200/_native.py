@@ -54,6 +54,11 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.csahca_csa_decode.argtypes = [_vp, _vp, _vp, _vp, _int, _int, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _vp,
                                       _sz, _vp]
 
+    lib.csahca_dsv4_indexer_workspace_size.restype = _sz
+    lib.csahca_dsv4_indexer_workspace_size.argtypes = [_i64, _i64]
+    lib.csahca_dsv4_indexer_topk.restype = _int
+    lib.csahca_dsv4_indexer_topk.argtypes = [_vp, _vp, _vp, _vp] + [_i64] * 5 + [_vp, _vp, _sz, _vp]
+
     lib.csahca_dsv4_decode.restype = _int
     lib.csahca_dsv4_decode.argtypes = [
         _vp, _int, _i64, _i64,          # q, q_dtype, num_queries, heads

@@ -1,0 +1,298 @@
+// DSV4 compressed-slot indexer: per-query index scores and top-k on device
+// (sm_100a, tcgen05).
+//
+// The reference takes the compressed (C4 / C128) slot indices of its DSV4
+// decode from its caller (integrations/sglang_dsv4/csahca_sglang_dsv4_patch/
+// patch.py:336-341) and lists an on-device indexer as future work
+// (docs/dsv4_abi_status.md:111-119).  This kernel computes them with the
+// published lightning-indexer score of DeepSeek-V3.2 (its technical report,
+// "DeepSeek Sparse Attention"):
+//     I[t, s] = sum_j  w[t, j] * ReLU(q[t, j, :] . k[s, :])
+// over H indexer heads j (q: [H, D] per query, w: [H] per query, k: one D-dim
+// indexer key per compressed slot s), then the top-k slots by I (largest
+// first, equal scores by lower slot, -1 past the valid count).
+//
+// Score kernel: one CTA per (query, run of 128-slot tiles).  Per tile,
+//   S^T[slot, head] = K[slot, :] . Q[head, :]       (M=128 slots, N=H heads, K=D)
+// runs as tcgen05.mma kind::f16 (bf16 in, fp32 accumulate in TMEM); each of
+// 128 epilogue threads owns one slot (TMEM lane) and reduces its row with the
+// weights and the ReLU.  Four producer warps copy the key tiles (rows of D
+// bf16, 256 B for D = 128) into 128-byte-swizzled shared memory with cp.async,
+// two tiles in flight.  Top-k kernel: one 1024-thread CTA per query over the
+// stored scores (the block top-k shared with the CSA scorers).
+#include <algorithm>
+
+#include "common.cuh"
+#include "sm100.cuh"
+#include "topk.cuh"
+
+namespace csahca {
+namespace {
+
+using namespace sm100;
+
+constexpr int kIdxHeads = 64;   // indexer heads (MMA N)
+constexpr int kIdxDim = 128;    // indexer head dim (MMA K total)
+constexpr int kTile = 128;      // slots per tile (MMA M)
+constexpr int kEpiWarps = 4;
+constexpr int kProdWarp0 = 4;
+constexpr int kProdWarps = 4;
+constexpr int kMmaWarp = kProdWarp0 + kProdWarps;
+constexpr int kThreads = (kMmaWarp + 1) * 32;  // 288
+constexpr int kTilesPerCta = 16;
+
+constexpr uint32_t kSubBytes = kTile * 128;                 // 16 KB: 128 slots x 64 dims
+constexpr uint32_t kKTileBytes = 2 * kSubBytes;             // 32 KB
+constexpr uint32_t kQSubBytes = kIdxHeads * 128;            // 8 KB: 64 heads x 64 dims
+constexpr uint32_t kOffQ = 0;
+constexpr uint32_t kOffK = kOffQ + 2 * kQSubBytes;
+constexpr uint32_t kOffBar = kOffK + 2 * kKTileBytes;
+constexpr uint32_t kSmemBytes = kOffBar + 1024 + 1024;      // barriers, weights + alignment slack
+constexpr uint32_t kTmemCols = 128;                         // two S^T buffers of 64 columns
+constexpr uint32_t kIdesc = idesc_bf16_f32(kTile, kIdxHeads, 0, 0);
+
+struct IdxBars {
+  uint64_t k_full[2], k_empty[2], s_full[2], s_empty[2];
+  uint32_t tmem_base;
+  int abort_flag;
+  float w[kIdxHeads];
+};
+
+struct IndexerParams {
+  const __nv_bfloat16* q;  // [Q, H, D]
+  const float* w;          // [Q, H]
+  const __nv_bfloat16* k;  // [Q, N, D]
+  const int32_t* lens;     // [Q] valid slots (nullptr: all N)
+  float* scores;           // [Q, N]
+  int num_queries, n_keys;
+  int* err;
+};
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ uint32_t sw128(int row, int c16) {
+  return uint32_t(row) * 128u + (uint32_t(c16 ^ (row & 7)) << 4);
+}
+
+__device__ __forceinline__ int valid_slots(const IndexerParams& p, int q) {
+  return p.lens != nullptr ? max(0, min(p.lens[q], p.n_keys)) : p.n_keys;
+}
+
+__global__ void __launch_bounds__(kThreads, 1) indexer_score_kernel(IndexerParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  IdxBars* bars = reinterpret_cast<IdxBars*>(smem + kOffBar);
+  const uint32_t q_base = smem_u32(smem + kOffQ), k_base = smem_u32(smem + kOffK);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  volatile int* abort_flag = &bars->abort_flag;
+  const int qi = blockIdx.y;
+  const int n = valid_slots(p, qi);
+  const int tile0 = blockIdx.x * kTilesPerCta;
+  const int ntiles = max(0, min(kTilesPerCta, (n + kTile - 1) / kTile - tile0));
+  if (ntiles == 0) return;  // uniform across the CTA, before any barrier
+
+  if (threadIdx.x == 0) {
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bars->k_full[b], kProdWarps * 32);
+      mbar_init(&bars->k_empty[b], 1);
+      mbar_init(&bars->s_full[b], 1);
+      mbar_init(&bars->s_empty[b], kEpiWarps * 32);
+    }
+    bars->abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (threadIdx.x < kIdxHeads) bars->w[threadIdx.x] = p.w[size_t(qi) * kIdxHeads + threadIdx.x];
+  if (warp == kMmaWarp) tmem_alloc(&bars->tmem_base, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+  bool failed = false;
+
+  if (warp >= kProdWarp0 && warp < kProdWarp0 + kProdWarps) {
+    // ------------------------------------------------------------ producers
+    // Chunk c (16 B) of a 256-byte key row goes to sub-tile c/8, swizzled
+    // chunk c%8 of the row; Q row pt/2 half pt%2 is copied once.  Rows past
+    // the valid count are zero-filled.
+    const int pt = threadIdx.x - kProdWarp0 * 32;
+    {
+      const int head = pt >> 1, half = pt & 1;
+      const __nv_bfloat16* src = p.q + (size_t(qi) * kIdxHeads + head) * kIdxDim + half * 64;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) cp_async16(q_base + uint32_t(half) * kQSubBytes + sw128(head, c), src + c * 8);
+    }
+    const __nv_bfloat16* kq = p.k + size_t(qi) * p.n_keys * kIdxDim;
+    // Key tiles: 16 consecutive threads copy one 256-byte row (chunk c = pt % 16),
+    // so every warp instruction reads 512 contiguous bytes.
+    const int c = pt & 15, r0 = pt >> 4;  // rows r0, r0 + 8, ..., r0 + 120
+    const uint32_t c_off = uint32_t(c >> 3) * kSubBytes;
+    bool ok = true;
+    for (int i = 0; i < ntiles && ok; ++i) {
+      const int b = i & 1;
+      if (i >= 2) ok = mbar_wait(&bars->k_empty[b], ((i >> 1) - 1) & 1, abort_flag);
+      if (!ok) break;
+      const int tile_slot = (tile0 + i) * kTile;
+      const uint32_t dst = k_base + uint32_t(b) * kKTileBytes + c_off;
+#pragma unroll
+      for (int j = 0; j < kTile / 8; ++j) {
+        const int row = r0 + 8 * j;
+        const uint32_t a = dst + sw128(row, c & 7);
+        if (tile_slot + row < n)
+          cp_async16(a, kq + size_t(tile_slot + row) * kIdxDim + c * 8);
+        else
+          asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(a), "r"(0u) : "memory");
+      }
+      cp_async_commit();
+      // The previous tile (and, with the first tile, Q) has landed: publish it.
+      if (i > 0) {
+        cp_async_wait<1>();
+        fence_proxy_async_smem();
+        mbar_arrive(&bars->k_full[(i - 1) & 1]);
+      }
+    }
+    if (ok) {
+      cp_async_wait<0>();
+      fence_proxy_async_smem();
+      mbar_arrive(&bars->k_full[(ntiles - 1) & 1]);
+    } else {
+      failed = true;
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      bool ok = true;
+      for (int i = 0; i < ntiles && ok; ++i) {
+        const int b = i & 1;
+        ok = mbar_wait(&bars->k_full[b], (i >> 1) & 1, abort_flag);
+        if (ok && i >= 2) ok = mbar_wait(&bars->s_empty[b], ((i >> 1) - 1) & 1, abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t kt = k_base + uint32_t(b) * kKTileBytes;
+#pragma unroll
+        for (int kk = 0; kk < kIdxDim / 16; ++kk) {
+          const uint32_t sub = uint32_t(kk >> 2), off = uint32_t(kk & 3) * 32u;
+          mma_bf16_ss(tmem + 64 * b, smem_desc_sw128(kt + sub * kSubBytes + off, 16, 1024),
+                      smem_desc_sw128(q_base + sub * kQSubBytes + off, 16, 1024), kIdesc, kk != 0);
+        }
+        mma_commit(&bars->s_full[b]);
+        mma_commit(&bars->k_empty[b]);
+      }
+      if (!ok) failed = true;
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue: one slot per thread
+    const int t = threadIdx.x;
+    const uint32_t t_lane = tmem + (uint32_t(warp * 32) << 16);
+    float* out = p.scores + size_t(qi) * p.n_keys;
+    for (int i = 0; i < ntiles; ++i) {
+      const int b = i & 1;
+      const bool ok = mbar_wait(&bars->s_full[b], (i >> 1) & 1, abort_flag);
+      if (!ok) {
+        failed = true;
+        break;
+      }
+      tc_fence_after();
+      float v[32];
+      float acc = 0.f;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        tmem_ld32(t_lane + 64 * b + 32 * h, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 32; ++c) acc = fmaf(bars->w[32 * h + c], fmaxf(v[c], 0.f), acc);
+      }
+      tc_fence_before();
+      mbar_arrive(&bars->s_empty[b]);
+      const int slot = (tile0 + i) * kTile + t;
+      if (slot < n) out[slot] = acc;
+    }
+  }
+  if (failed) {
+    *abort_flag = 1;
+    report_device_error(p.err, kErrWaitTimeout);
+  }
+  tc_fence_before();
+  asm volatile("barrier.sync 0;" ::: "memory");
+  tc_fence_after();
+  if (warp == kMmaWarp) {
+    __syncwarp();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+constexpr int kTopkThreads = 1024;
+
+// Top-k of query blockIdx.x's valid scores (largest first, ties to the lower
+// slot, -1 past the valid count); leaves its scores zero.
+__global__ void __launch_bounds__(kTopkThreads) indexer_topk_kernel(IndexerParams p, int kout, int32_t* out) {
+  __shared__ unsigned long long s_red[kTopkThreads / 32];
+  __shared__ unsigned s_hist[256];
+  __shared__ unsigned s_misc[4];
+  __shared__ unsigned long long s_keys[kTopkThreads];
+  const int qi = blockIdx.x;
+  const int n = valid_slots(p, qi);
+  float* sc = p.scores + size_t(qi) * p.n_keys;
+  if (n <= kTopkThreads * 16 && kout <= kTopkThreads)
+    topk::block_topk_radix<kTopkThreads, 16>(sc, n, kout, out + size_t(qi) * kout, s_hist, s_keys, s_misc);
+  else
+    topk::block_topk<kTopkThreads>(sc, n, kout, out + size_t(qi) * kout, s_red);
+}
+
+}  // namespace
+}  // namespace csahca
+
+using namespace csahca;
+
+extern "C" size_t csahca_dsv4_indexer_workspace_size(int64_t num_queries, int64_t n_keys) {
+  if (num_queries <= 0 || n_keys <= 0) return 256;
+  return ((size_t(num_queries) * size_t(n_keys) * 4 + 255) & ~size_t(255));
+}
+
+extern "C" int csahca_dsv4_indexer_topk(const void* q, const float* weights, const void* keys,
+                                        const int32_t* key_lens, int64_t num_queries, int64_t heads,
+                                        int64_t n_keys, int64_t head_dim, int64_t top_k, int32_t* out_indices,
+                                        void* workspace, size_t workspace_bytes, void* stream) {
+  if (heads != kIdxHeads || head_dim != kIdxDim)
+    return csahca_set_unsupported("the indexer supports 64 heads of dim 128");
+  if (num_queries < 0 || n_keys < 0 || top_k <= 0) return csahca_set_arg_error("sizes must be non-negative, top_k positive");
+  const int64_t kout = std::min<int64_t>(top_k, n_keys);
+  if (num_queries == 0 || kout == 0) return CSAHCA_OK;
+  if (num_queries > 65535) return csahca_set_unsupported("at most 65535 queries per call");
+  if (n_keys * num_queries > (int64_t(1) << 31)) return csahca_set_unsupported("problem too large");
+  if (workspace_bytes < csahca_dsv4_indexer_workspace_size(num_queries, n_keys))
+    return csahca_set_arg_error("workspace too small");
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(keys)) & 15)
+    return csahca_set_arg_error("q and keys must be 16-byte aligned");
+  IndexerParams p;
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.w = weights;
+  p.k = static_cast<const __nv_bfloat16*>(keys);
+  p.lens = key_lens;
+  p.scores = static_cast<float*>(workspace);
+  p.num_queries = int(num_queries);
+  p.n_keys = int(n_keys);
+  p.err = csahca_device_error_ptr();
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  static bool configured[64] = {};
+  int dev = 0;
+  CSAHCA_RETURN_IF_CUDA(cudaGetDevice(&dev));
+  if (dev < 64 && !configured[dev]) {
+    CSAHCA_RETURN_IF_CUDA(
+        cudaFuncSetAttribute(indexer_score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes)));
+    configured[dev] = true;
+  }
+  const int tiles = int((n_keys + kTile - 1) / kTile);
+  const dim3 grid(unsigned((tiles + kTilesPerCta - 1) / kTilesPerCta), unsigned(num_queries));
+  indexer_score_kernel<<<grid, kThreads, kSmemBytes, s>>>(p);
+  CSAHCA_RETURN_IF_CUDA(cudaGetLastError());
+  indexer_topk_kernel<<<unsigned(num_queries), kTopkThreads, 0, s>>>(p, int(kout), out_indices);
+  CSAHCA_RETURN_IF_CUDA(cudaGetLastError());
+  return CSAHCA_OK;
+}

@@ -205,5 +205,43 @@ def csa_decode_step(q, k_cache, v_cache, chunk_size: int, top_k: int,
     return csa_decode_forward_tiled(q, k_cache, v_cache, selected, chunk_size), selected
 
 
+def dsv4_indexer_topk(q_idx: torch.Tensor, weights: torch.Tensor, keys: torch.Tensor, top_k: int,
+                      key_lens: torch.Tensor | None = None) -> torch.Tensor:
+    """Compressed-slot indices for the DSV4 decode, selected on the GPU.
+
+    Per query t the index score of key slot s is
+    ``sum_j weights[t, j] * relu(q_idx[t, j] . keys[t, s])`` (the lightning
+    indexer of the DeepSeek-V3.2 report); returns int32 ``[Q, min(top_k, N)]``
+    slot positions, largest score first, equal scores by lower slot, -1 past
+    ``key_lens[t]``.  ``q_idx`` bf16 ``[Q, 64, 128]``, ``weights`` fp32 ``[Q, 64]``,
+    ``keys`` bf16 ``[Q, N, 128]``.  The reference receives these indices from
+    its caller (integrations/sglang_dsv4/csahca_sglang_dsv4_patch/patch.py:336-341).
+    """
+    if q_idx.ndim != 3 or keys.ndim != 3 or weights.ndim != 2:
+        raise ValueError("q_idx must be [Q,H,D], weights [Q,H], keys [Q,N,D]")
+    if q_idx.shape[0] != keys.shape[0] or q_idx.shape[2] != keys.shape[2] or weights.shape != q_idx.shape[:2]:
+        raise ValueError("q_idx, weights and keys dimensions must match")
+    if q_idx.dtype != torch.bfloat16 or keys.dtype != torch.bfloat16:
+        raise ValueError("q_idx and keys must be bfloat16")
+    if not (q_idx.is_cuda and keys.is_cuda and weights.is_cuda):
+        raise RuntimeError("dsv4_indexer_topk: tensors must be CUDA tensors")
+    lib = N.lib()
+    q_idx, keys = q_idx.contiguous(), keys.contiguous()
+    weights = weights.to(torch.float32).contiguous()
+    nq, heads, d = q_idx.shape
+    n = keys.shape[1]
+    out = torch.empty((nq, min(int(top_k), n)), dtype=torch.int32, device=q_idx.device)
+    if key_lens is not None:
+        key_lens = key_lens.to(device=q_idx.device, dtype=torch.int32).contiguous()
+        if key_lens.numel() != nq:
+            raise ValueError("key_lens must have one value per query")
+    with torch.cuda.device(q_idx.device):
+        ws = N.workspaces.get(q_idx.device, lib.csahca_dsv4_indexer_workspace_size(nq, n), "dsv4_indexer")
+        N.check(lib.csahca_dsv4_indexer_topk(
+            q_idx.data_ptr(), weights.data_ptr(), keys.data_ptr(), N.ptr(key_lens), nq, heads, n, d, int(top_k),
+            out.data_ptr(), ws.data_ptr(), ws.numel(), N.stream_handle(q_idx.device)))
+    return out
+
+
 def default_dsv4_softmax_scale() -> float:
     return 1.0 / math.sqrt(512)

@@ -147,6 +147,26 @@ int csahca_csa_decode_noalloc(const void* q, const void* k_cache, const void* v_
                               int index_dtype, int dtype, int64_t batch, int64_t heads, int64_t seq_len,
                               int64_t head_dim, int64_t top_k, int64_t chunk_size, void* out, void* stream);
 
+/* ------------------------------------------------------------------ DSV4 indexer
+ * Compressed-slot selection on device: per query, index scores
+ *   I[s] = sum_j w[j] * max(0, q[j, :] . k[s, :])
+ * over its indexer heads j and key slots s (the lightning-indexer score of
+ * the DeepSeek-V3.2 technical report), then the top_k slots by I, largest
+ * first, equal scores by lower slot, -1 past min(top_k, valid slots).  The
+ * reference has no counterpart: its DSV4 path receives these indices from its
+ * caller (integrations/sglang_dsv4/csahca_sglang_dsv4_patch/patch.py:336-341)
+ * and lists an on-device indexer as future work (docs/dsv4_abi_status.md:111-119).
+ *
+ * q [Q, 64, 128] bf16, weights [Q, 64] fp32, keys [Q, n_keys, 128] bf16 (each
+ * query's compressed-slot keys), key_lens [Q] int32 valid slots (NULL: all);
+ * out_indices [Q, min(top_k, n_keys)] int32.  workspace:
+ * csahca_dsv4_indexer_workspace_size() bytes of any content.
+ */
+size_t csahca_dsv4_indexer_workspace_size(int64_t num_queries, int64_t n_keys);
+int csahca_dsv4_indexer_topk(const void* q, const float* weights, const void* keys, const int32_t* key_lens,
+                             int64_t num_queries, int64_t heads, int64_t n_keys, int64_t head_dim, int64_t top_k,
+                             int32_t* out_indices, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------ DSV4 decode
  * DeepSeek-V4 paged FP8 latent-cache decode (compress ratio 0 / 4 / 128).
  * Replaces csrc/dsv4_attention.cu:585-657 (dsv4_swa_decode_forward_cuda),
