@@ -84,7 +84,7 @@ __device__ __forceinline__ int valid_slots(const IndexerParams& p, int q) {
   return p.lens != nullptr ? max(0, min(p.lens[q], p.n_keys)) : p.n_keys;
 }
 
-__global__ void __launch_bounds__(kThreads, 1) indexer_score_kernel(IndexerParams p) {
+__global__ void __launch_bounds__(kThreads, 2) indexer_score_kernel(IndexerParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   IdxBars* bars = reinterpret_cast<IdxBars*>(smem + kOffBar);
