@@ -94,3 +94,18 @@ def test_indexer_rejects_unsupported_shapes(cuda):
     with pytest.raises(RuntimeError, match="64 heads of dim 128"):
         ext.dsv4_indexer_topk(q, torch.zeros(1, 32, device=cuda), torch.zeros(1, 8, 128, dtype=torch.bfloat16,
                                                                               device=cuda), 4)
+
+
+def test_indexer_validates_before_any_launch():
+    """Shape, dtype and device errors are raised in Python, before the library runs."""
+    from csahca_b200 import extension as ext
+
+    q = torch.zeros(2, 64, 128, dtype=torch.bfloat16)
+    w = torch.zeros(2, 64)
+    keys = torch.zeros(2, 300, 128, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="must be CUDA tensors"):
+        ext.dsv4_indexer_topk(q, w, keys, 8)
+    with pytest.raises(ValueError, match="bfloat16"):
+        ext.dsv4_indexer_topk(q.float(), w, keys, 8)
+    with pytest.raises(ValueError, match="dimensions must match"):
+        ext.dsv4_indexer_topk(q, w[:1], keys, 8)
