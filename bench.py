@@ -1,7 +1,7 @@
 """Benchmark of the CSA / DSV4 decode path on B200 (one process per GPU).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload csa_batched|csa_cfg1|dsv4_c0|dsv4_c4|dsv4_c128|dsv4_splitkv]
+                    [--workload csa_batched|csa_cfg1|dsv4_c0|dsv4_c4|dsv4_c128|dsv4_splitkv|dsv4_indexer]
 
 Default workload (the metric's batched case): one
 dynamic CSA decode step for a batch of 64 requests x 32 heads, head_dim 128,
@@ -16,7 +16,8 @@ requests is split over the ranks greedily by context length (sum of L_b per
 rank balanced, ``csahca_b200.partition``); every rank materialises and decodes
 only its share, with no collective on the data path.  ``value`` = 64 requests
 / the step time, max over ranks.  ``--workload dsv4_c*`` splits the DSV4 batch
-by query (Q/N per rank) and ``csa_cfg1`` splits config 1's 8 heads.
+by query (Q/N per rank), ``dsv4_indexer`` splits the config-5 indexer by
+query and ``csa_cfg1`` splits config 1's 8 heads.
 
 At N=1 the line also carries ``secondary``: DSV4 decode (configs 4 and 5: C0,
 C4, C128), config 1 and the config-3 mini block, each timed alone with CUDA
@@ -610,6 +611,29 @@ def bench_dsv4_sharded(dev, rank: int, world: int, workload: str, steps: int, wa
             "h2d": q_host.numel() * 2, "d2h": out_host.numel() * 2}
 
 
+def bench_indexer_sharded(dev, rank: int, world: int, steps: int, warmup: int, queries: int = 0) -> dict:
+    """DSV4 indexer (score + top-64 over 16384 C4 slots, config 5's shape) split
+    by query over the ranks, no collective; step time = max over ranks."""
+    from csahca_b200 import extension as ext
+    from csahca_b200 import partition as P
+
+    nq_total, n, top_k = queries or 256, 16384, 64
+    mine = P.shard_queries(nq_total, rank, world)
+    nq = len(mine)
+    g = torch.Generator(device=dev).manual_seed(5 + rank)
+    q = torch.randn(nq, 64, 128, generator=g, device=dev).to(torch.bfloat16)
+    w = torch.randn(nq, 64, generator=g, device=dev) * 0.1
+    keys = torch.randn(nq, n, 128, generator=g, device=dev, dtype=torch.bfloat16)
+    _barrier(world)
+    with ClockSampler(dev.index) as clk:
+        ms_own = _time_flushed(lambda: ext.dsv4_indexer_topk(q, w, keys, top_k), dev, iters=steps,
+                               warm=max(3, warmup))
+    nb = keys.numel() * 2 + q.numel() * 2 + w.numel() * 4 + nq * top_k * 4
+    return {"ms": _max_over_ranks(ms_own, dev, world), "clocks": clk.summary(), "queries": nq,
+            "nq_total": nq_total, "achieved_gbs": round(nb / (ms_own / 1e3) / 1e9, 1),
+            "hbm_frac": round(nb / (ms_own / 1e3) / 1e9 / _peaks()[0], 4), "algorithmic_bytes": nb}
+
+
 def bench_cfg1_sharded(dev, rank: int, world: int, steps: int, warmup: int) -> dict:
     """Config 1 (one request, 8 heads) split by head: rank r scores, selects and
     decodes heads [8r/N, 8(r+1)/N).  L2 flushed before every step."""
@@ -657,9 +681,10 @@ def main() -> int:
     ap.add_argument("--cpu-requests", type=int, default=0,
                     help="config-2 requests in one CPU sample (default: one per host core, at most 16)")
     ap.add_argument("--workload", choices=["csa_batched", "csa_cfg1", "dsv4_c0", "dsv4_c4", "dsv4_c128",
-                                           "dsv4_splitkv"], default="csa_batched",
+                                           "dsv4_splitkv", "dsv4_indexer"], default="csa_batched",
                     help="csa_cfg1: config 1 split by head; dsv4_c*: that DSV4 batch split by query; "
-                         "dsv4_splitkv: one config-5 request (C4) split across the ranks with an NCCL all-gather")
+                         "dsv4_splitkv: one config-5 request (C4) split across the ranks with an NCCL all-gather; "
+                         "dsv4_indexer: the config-5 indexer (score + top-64) split by query")
     ap.add_argument("--batch", type=int, default=64, help="csa_batched: override the batch (profiling only)")
     ap.add_argument("--queries", type=int, default=0, help="dsv4_*: override the number of queries")
     ap.add_argument("--context", type=int, default=0, help="dsv4_c4/c128: override the per-request context")
@@ -724,6 +749,22 @@ def _run(a, dev, rank: int, world: int, cores: int, cpu_requests: int) -> int:
                               "config": {"workload": "csa_cfg1 (BASELINE config 1: B1 H8 S32768 D128 c64 k8)",
                                          "parallelism": f"head-sharded over {world} GPUs, no collective",
                                          "heads_per_rank_0": r["heads"], "l2": "flushed before every step"},
+                              "gpu_launches": 2 * a.steps, "clocks": r["clocks"]}), flush=True)
+        return 0
+    if a.workload == "dsv4_indexer":
+        r = bench_indexer_sharded(dev, rank, world, a.steps, a.warmup, a.queries)
+        if rank == 0:
+            ms = r["ms"]
+            print(json.dumps({"metric": "DSV4 indexer throughput (score + top-64), config 5 shape",
+                              "value": round(r["nq_total"] / (ms / 1e3), 1), "unit": UNIT, **common,
+                              "ms_per_step": round(ms, 5), "us_per_step": round(ms * 1e3, 2),
+                              "config": {"workload": f"dsv4_indexer (Q{r['nq_total']}, 16384 C4 slots, "
+                                                     "64 x 128 indexer heads, top-64)",
+                                         "parallelism": f"query-sharded over {world} GPUs, no collective",
+                                         "l2": "flushed before every step"},
+                              "roofline": {"bound": "hbm", "kernel": "indexer_score_kernel + indexer_topk_kernel",
+                                           "achieved": r["achieved_gbs"], "peak": _peaks()[0], "unit": "GB/s",
+                                           "frac": r["hbm_frac"], "traffic": None},
                               "gpu_launches": 2 * a.steps, "clocks": r["clocks"]}), flush=True)
         return 0
     if a.workload != "csa_batched":

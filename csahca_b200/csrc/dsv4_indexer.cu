@@ -227,22 +227,29 @@ __global__ void __launch_bounds__(kThreads, 2) indexer_score_kernel(IndexerParam
   }
 }
 
-constexpr int kTopkThreads = 1024;
+constexpr int kTopkThreads = 512;  // two CTAs per SM: 256 queries in one wave
+constexpr int kTopkPer = 32;       // radix path: up to 16384 slots in registers
 
 // Top-k of query blockIdx.x's valid scores (largest first, ties to the lower
-// slot, -1 past the valid count); leaves its scores zero.
-__global__ void __launch_bounds__(kTopkThreads) indexer_topk_kernel(IndexerParams p, int kout, int32_t* out) {
-  __shared__ unsigned long long s_red[kTopkThreads / 32];
-  __shared__ unsigned s_hist[256];
+// slot, -1 past the valid count), by radix selection: n_keys <= 16384 and
+// top_k <= 512.
+__global__ void __launch_bounds__(kTopkThreads, 2) indexer_topk_kernel(IndexerParams p, int kout, int32_t* out) {
+  __shared__ unsigned s_hist[4096];
+  __shared__ unsigned s_wsum[kTopkThreads / 32];
   __shared__ unsigned s_misc[4];
   __shared__ unsigned long long s_keys[kTopkThreads];
   const int qi = blockIdx.x;
-  const int n = valid_slots(p, qi);
-  float* sc = p.scores + size_t(qi) * p.n_keys;
-  if (n <= kTopkThreads * 16 && kout <= kTopkThreads)
-    topk::block_topk_radix<kTopkThreads, 16>(sc, n, kout, out + size_t(qi) * kout, s_hist, s_keys, s_misc);
-  else
-    topk::block_topk<kTopkThreads>(sc, n, kout, out + size_t(qi) * kout, s_red);
+  topk::block_topk_radix<kTopkThreads, kTopkPer>(p.scores + size_t(qi) * p.n_keys, valid_slots(p, qi), kout,
+                                                 out + size_t(qi) * kout, s_hist, s_wsum, s_keys, s_misc);
+}
+
+// Same result for any n_keys and top_k, one selection round per output (leaves
+// the scores zero; the score kernel rewrites them on every call).
+__global__ void __launch_bounds__(kTopkThreads) indexer_topk_rounds_kernel(IndexerParams p, int kout, int32_t* out) {
+  __shared__ unsigned long long s_red[kTopkThreads / 32];
+  const int qi = blockIdx.x;
+  topk::block_topk<kTopkThreads>(p.scores + size_t(qi) * p.n_keys, valid_slots(p, qi), kout,
+                                 out + size_t(qi) * kout, s_red);
 }
 
 }  // namespace
@@ -292,7 +299,10 @@ extern "C" int csahca_dsv4_indexer_topk(const void* q, const float* weights, con
   const dim3 grid(unsigned((tiles + kTilesPerCta - 1) / kTilesPerCta), unsigned(num_queries));
   indexer_score_kernel<<<grid, kThreads, kSmemBytes, s>>>(p);
   CSAHCA_RETURN_IF_CUDA(cudaGetLastError());
-  indexer_topk_kernel<<<unsigned(num_queries), kTopkThreads, 0, s>>>(p, int(kout), out_indices);
+  if (n_keys <= int64_t(kTopkThreads) * kTopkPer && kout <= kTopkThreads)
+    indexer_topk_kernel<<<unsigned(num_queries), kTopkThreads, 0, s>>>(p, int(kout), out_indices);
+  else
+    indexer_topk_rounds_kernel<<<unsigned(num_queries), kTopkThreads, 0, s>>>(p, int(kout), out_indices);
   CSAHCA_RETURN_IF_CUDA(cudaGetLastError());
   return CSAHCA_OK;
 }

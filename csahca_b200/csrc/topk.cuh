@@ -75,71 +75,114 @@ __device__ void block_topk(float* scores, int n, int kout, int32_t* out, unsigne
 namespace csahca {
 namespace topk {
 
-// Top-k by radix selection, for n <= kThreads * kPer and kout <= kThreads:
-// every element gets the unique 64-bit key (order-preserving score bits,
-// ~index), so the k largest keys are exactly the k largest scores with ties
-// to the lower index.  Eight passes of an 8-bit histogram (shared memory)
-// narrow the key prefix to the k-th largest key; the elements at or above it
-// are compacted and sorted descending by a bitonic network.  Same results as
-// block_topk.  s_hist: 256 unsigned; s_keys: kThreads unsigned long long.
+// Top-k by radix selection, for n <= kThreads * kPer and kout <= kThreads.
+// Every element has the unique 64-bit key (order-preserving score bits, ~index),
+// so the k largest keys are exactly the k largest scores with ties to the lower
+// index.  Registers hold only the 32 score bits; element i = e * kThreads + tid,
+// so the index half of a key follows from the position.  Histogram passes over
+// digits of 12, 12 and 8 bits (then 8-bit digits of the index, reached only by
+// equal scores) narrow the key prefix; a pass whose chosen bin is wanted whole
+// ends the search early, since every key in it is then taken.  The keys at or
+// above the final prefix are compacted and sorted descending by a bitonic
+// network.  Same results as block_topk.
+// Shared memory: s_hist 4096 unsigned, s_wsum kThreads/32 unsigned,
+// s_keys kThreads unsigned long long, s_misc 4 unsigned.
 template <int kThreads, int kPer>
 __device__ void block_topk_radix(const float* scores, int n, int kout, int32_t* out, unsigned* s_hist,
-                                 unsigned long long* s_keys, unsigned* s_misc) {
-  const int tid = threadIdx.x;
-  unsigned long long keys[kPer];
+                                 unsigned* s_wsum, unsigned long long* s_keys, unsigned* s_misc) {
+  constexpr int kWarps = kThreads / 32;
+  static_assert(kWarps <= 32 && kThreads % 32 == 0, "one warp scans the warp totals");
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  uint32_t sk[kPer];
 #pragma unroll
   for (int e = 0; e < kPer; ++e) {
-    const int i = tid * kPer + e;  // consecutive elements per thread: coalesced enough from L2
-    keys[e] = i < n ? make_key(__ldcg(scores + i), i) : 0ull;
+    const int i = e * kThreads + tid;
+    sk[e] = i < n ? float_order_key(__ldcg(scores + i)) : 0u;
   }
   const int kvalid = min(kout, n);
-  unsigned long long prefix = 0ull, mask = 0ull;
-  int need = kvalid;  // how many keys >= the threshold remain to be found in the current bin
-  for (int pass = 0; pass < 8 && kvalid > 0; ++pass) {
-    const int shift = 56 - 8 * pass;
-    for (int b = tid; b < 256; b += kThreads) s_hist[b] = 0u;
+  // The key prefix found so far, as its score half and its ~index half.
+  uint32_t pre_hi = 0u, msk_hi = 0u, pre_lo = 0u, msk_lo = 0u;
+  int need = kvalid;  // keys still wanted from the keys that match the prefix
+  bool done = kvalid <= 0;
+#pragma unroll 1
+  for (int pass = 0; pass < 7; ++pass) {
+    if (done) break;
+    const int bits = pass < 2 ? 12 : 8;
+    const int shift = pass == 0 ? 20 : pass == 1 ? 8 : pass == 2 ? 0 : 24 - 8 * (pass - 3);  // within its half
+    const bool hi = pass < 3;
+    const int nb = 1 << bits;
+    const int per = nb >= kThreads ? nb / kThreads : 1;
+    for (int b = tid; b < nb; b += kThreads) s_hist[b] = 0u;
     __syncthreads();
 #pragma unroll
-    for (int e = 0; e < kPer; ++e)
-      if (tid * kPer + e < n && (keys[e] & mask) == prefix) atomicAdd(&s_hist[(keys[e] >> shift) & 0xFF], 1u);
-    __syncthreads();
-    if (tid < 32) {
-      // Bin holding the need-th largest key among the prefix matches, from the top.
-      unsigned cnt[8];
-      unsigned tot = 0;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        cnt[j] = s_hist[255 - (8 * tid + j)];
-        tot += cnt[j];
-      }
-      unsigned incl = tot;  // inclusive prefix over lanes (bins from the top)
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const unsigned v = __shfl_up_sync(0xffffffffu, incl, o);
-        if (tid >= o) incl += v;
-      }
-      unsigned run = incl - tot;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if (run < unsigned(need) && run + cnt[j] >= unsigned(need)) {
-          s_misc[0] = unsigned(255 - (8 * tid + j));
-          s_misc[1] = unsigned(need) - run;  // still needed inside this bin
-        }
-        run += cnt[j];
-      }
+    for (int e = 0; e < kPer; ++e) {
+      const int i = e * kThreads + tid;
+      const uint32_t lo = ~static_cast<uint32_t>(i);
+      if (i < n && (sk[e] & msk_hi) == pre_hi && (lo & msk_lo) == pre_lo)
+        atomicAdd(&s_hist[((hi ? sk[e] : lo) >> shift) & uint32_t(nb - 1)], 1u);
     }
     __syncthreads();
-    prefix |= static_cast<unsigned long long>(s_misc[0]) << shift;
-    mask |= 0xFFull << shift;
-    need = int(s_misc[1]);
+    // Bins from the top: thread t owns bins nb-1-(t*per) down to nb-(t+1)*per.
+    unsigned tot = 0;
+    const bool owns = tid * per < nb;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (j < per && owns) tot += s_hist[nb - 1 - (tid * per + j)];
+    unsigned incl = tot;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const unsigned v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    if (lane == 31) s_wsum[warp] = incl;
     __syncthreads();
+    if (warp == 0) {
+      const unsigned w = lane < kWarps ? s_wsum[lane] : 0u;
+      unsigned wi = w;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned v = __shfl_up_sync(0xffffffffu, wi, o);
+        if (lane >= o) wi += v;
+      }
+      __syncwarp();
+      if (lane < kWarps) s_wsum[lane] = wi - w;  // exclusive prefix of the warp totals
+    }
+    __syncthreads();
+    unsigned run = s_wsum[warp] + incl - tot;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (!(j < per && owns)) continue;
+      const unsigned c = s_hist[nb - 1 - (tid * per + j)];
+      if (run < unsigned(need) && run + c >= unsigned(need)) {
+        s_misc[0] = unsigned(nb - 1 - (tid * per + j));
+        s_misc[1] = unsigned(need) - run;
+        s_misc[3] = (run + c == unsigned(need)) ? 1u : 0u;
+      }
+      run += c;
+    }
+    __syncthreads();
+    if (hi) {
+      pre_hi |= s_misc[0] << shift;
+      msk_hi |= uint32_t(nb - 1) << shift;
+    } else {
+      pre_lo |= s_misc[0] << shift;
+      msk_lo |= uint32_t(nb - 1) << shift;
+    }
+    need = int(s_misc[1]);
+    done = s_misc[3] != 0u;
   }
-  // prefix is now the kvalid-th largest key: compact every key >= it.
+  // Exactly kvalid keys are >= the prefix (lower bits zero when the search ended early).
+  const unsigned long long prefix = (static_cast<unsigned long long>(pre_hi) << 32) | pre_lo;
   if (tid == 0) s_misc[2] = 0u;
   __syncthreads();
+  if (kvalid > 0) {
 #pragma unroll
-  for (int e = 0; e < kPer; ++e)
-    if (kvalid > 0 && tid * kPer + e < n && keys[e] >= prefix) s_keys[atomicAdd(&s_misc[2], 1u)] = keys[e];
+    for (int e = 0; e < kPer; ++e) {
+      const int i = e * kThreads + tid;
+      const unsigned long long k = (static_cast<unsigned long long>(sk[e]) << 32) | ~static_cast<uint32_t>(i);
+      if (i < n && k >= prefix) s_keys[atomicAdd(&s_misc[2], 1u)] = k;
+    }
+  }
   __syncthreads();
   int m = 1;
   while (m < kvalid) m <<= 1;

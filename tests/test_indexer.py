@@ -87,6 +87,32 @@ def test_indexer_matches_oracle(cuda, nq, n, top_k, ragged):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("nq,n,top_k", [(3, 16384, 512), (2, 16384, 64), (2, 20000, 64), (2, 3000, 600),
+                                        (2, 700, 700)])
+def test_indexer_ties_exact(cuda, nq, n, top_k):
+    """Scores that are small integers (exact in fp32 whatever the summation
+    order) with heavy ties: the selection must equal the oracle's bit for bit,
+    equal scores ordered by the lower slot.  Covers the radix path (its index
+    digits are reached only through ties) and the per-round fallback (more
+    than 16384 slots, top_k above 512)."""
+    from csahca_b200 import extension as ext
+
+    rng = np.random.default_rng(n + top_k)
+    q32 = np.zeros((nq, 64, 128), np.float32)
+    q32[:, :, 0] = 1.0
+    k32 = np.zeros((nq, n, 128), np.float32)
+    k32[:, :, 0] = rng.integers(-3, 4, (nq, n))
+    k32[0] = 0.0  # query 0: every score equal
+    q, keys = from_f32(q32, "bf16"), from_f32(k32, "bf16")
+    w = rng.integers(1, 3, (nq, 64)).astype(np.float32)
+    want = indexer.indexer_topk(q, w, keys, top_k)
+    got = ext.dsv4_indexer_topk(to_torch(q, "bf16", cuda), torch.from_numpy(w).to(cuda),
+                                to_torch(keys, "bf16", cuda), top_k).cpu().numpy()
+    np.testing.assert_array_equal(got, want)
+    np.testing.assert_array_equal(got[0, :min(top_k, n)], np.arange(min(top_k, n)))
+
+
+@pytest.mark.gpu
 def test_indexer_rejects_unsupported_shapes(cuda):
     from csahca_b200 import extension as ext
 
