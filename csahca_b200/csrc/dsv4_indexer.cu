@@ -228,19 +228,20 @@ __global__ void __launch_bounds__(kThreads, 2) indexer_score_kernel(IndexerParam
 }
 
 constexpr int kTopkThreads = 512;  // two CTAs per SM: 256 queries in one wave
-constexpr int kTopkPer = 32;       // radix path: up to 16384 slots in registers
+constexpr int kTopkMaxSlots = 49152;  // radix path: the scores of one query staged in shared memory
 
 // Top-k of query blockIdx.x's valid scores (largest first, ties to the lower
-// slot, -1 past the valid count), by radix selection: n_keys <= 16384 and
-// top_k <= 512.
+// slot, -1 past the valid count), by radix selection: n_keys <= 49152 and
+// top_k <= 512.  Dynamic shared memory: n_keys words.
 __global__ void __launch_bounds__(kTopkThreads, 2) indexer_topk_kernel(IndexerParams p, int kout, int32_t* out) {
+  extern __shared__ uint32_t s_sk[];
   __shared__ unsigned s_hist[4096];
   __shared__ unsigned s_wsum[kTopkThreads / 32];
   __shared__ unsigned s_misc[4];
   __shared__ unsigned long long s_keys[kTopkThreads];
   const int qi = blockIdx.x;
-  topk::block_topk_radix<kTopkThreads, kTopkPer>(p.scores + size_t(qi) * p.n_keys, valid_slots(p, qi), kout,
-                                                 out + size_t(qi) * kout, s_hist, s_wsum, s_keys, s_misc);
+  topk::block_topk_radix<kTopkThreads>(p.scores + size_t(qi) * p.n_keys, valid_slots(p, qi), kout,
+                                       out + size_t(qi) * kout, s_sk, s_hist, s_wsum, s_keys, s_misc);
 }
 
 // Same result for any n_keys and top_k, one selection round per output (leaves
@@ -293,14 +294,16 @@ extern "C" int csahca_dsv4_indexer_topk(const void* q, const float* weights, con
   if (dev < 64 && !configured[dev]) {
     CSAHCA_RETURN_IF_CUDA(
         cudaFuncSetAttribute(indexer_score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes)));
+    CSAHCA_RETURN_IF_CUDA(cudaFuncSetAttribute(indexer_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               kTopkMaxSlots * 4));
     configured[dev] = true;
   }
   const int tiles = int((n_keys + kTile - 1) / kTile);
   const dim3 grid(unsigned((tiles + kTilesPerCta - 1) / kTilesPerCta), unsigned(num_queries));
   indexer_score_kernel<<<grid, kThreads, kSmemBytes, s>>>(p);
   CSAHCA_RETURN_IF_CUDA(cudaGetLastError());
-  if (n_keys <= int64_t(kTopkThreads) * kTopkPer && kout <= kTopkThreads)
-    indexer_topk_kernel<<<unsigned(num_queries), kTopkThreads, 0, s>>>(p, int(kout), out_indices);
+  if (n_keys <= kTopkMaxSlots && kout <= kTopkThreads)
+    indexer_topk_kernel<<<unsigned(num_queries), kTopkThreads, size_t(n_keys) * 4, s>>>(p, int(kout), out_indices);
   else
     indexer_topk_rounds_kernel<<<unsigned(num_queries), kTopkThreads, 0, s>>>(p, int(kout), out_indices);
   CSAHCA_RETURN_IF_CUDA(cudaGetLastError());

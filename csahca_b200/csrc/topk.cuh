@@ -75,51 +75,48 @@ __device__ void block_topk(float* scores, int n, int kout, int32_t* out, unsigne
 namespace csahca {
 namespace topk {
 
-// Top-k by radix selection, for n <= kThreads * kPer and kout <= kThreads.
-// Every element has the unique 64-bit key (order-preserving score bits, ~index),
-// so the k largest keys are exactly the k largest scores with ties to the lower
-// index.  Registers hold only the 32 score bits; element i = e * kThreads + tid,
-// so the index half of a key follows from the position.  Histogram passes over
-// digits of 12, 12 and 8 bits (then 8-bit digits of the index, reached only by
-// equal scores) narrow the key prefix; a pass whose chosen bin is wanted whole
-// ends the search early, since every key in it is then taken.  The keys at or
-// above the final prefix are compacted and sorted descending by a bitonic
-// network.  Same results as block_topk.
-// Shared memory: s_hist 4096 unsigned, s_wsum kThreads/32 unsigned,
-// s_keys kThreads unsigned long long, s_misc 4 unsigned.
-template <int kThreads, int kPer>
-__device__ void block_topk_radix(const float* scores, int n, int kout, int32_t* out, unsigned* s_hist,
-                                 unsigned* s_wsum, unsigned long long* s_keys, unsigned* s_misc) {
+// Top-k by radix selection, for kout <= kThreads.  Every element has the
+// unique 64-bit key (order-preserving score bits, ~index), so the k largest
+// keys are exactly the k largest scores with ties to the lower index.  The
+// score halves are staged once in shared memory (s_sk, n words); the index
+// half follows from the position.  Histogram passes over digits of 12, 12 and
+// 8 bits (then 8-bit digits of the index, reached only by equal scores) narrow
+// the key prefix; a pass whose chosen bin is wanted whole ends the search
+// early, since every key in it is then taken.  The keys at or above the final
+// prefix are compacted and each is written at its rank among them.  Same
+// results as block_topk.
+// Shared memory: s_sk n words, s_hist 4096 unsigned, s_wsum kThreads/32
+// unsigned, s_keys kThreads unsigned long long, s_misc 4 unsigned.
+template <int kThreads>
+__device__ void block_topk_radix(const float* scores, int n, int kout, int32_t* out, uint32_t* s_sk,
+                                 unsigned* s_hist, unsigned* s_wsum, unsigned long long* s_keys, unsigned* s_misc) {
   constexpr int kWarps = kThreads / 32;
   static_assert(kWarps <= 32 && kThreads % 32 == 0, "one warp scans the warp totals");
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  uint32_t sk[kPer];
-#pragma unroll
-  for (int e = 0; e < kPer; ++e) {
-    const int i = e * kThreads + tid;
-    sk[e] = i < n ? float_order_key(__ldcg(scores + i)) : 0u;
-  }
+  for (int i = tid; i < n; i += kThreads) s_sk[i] = float_order_key(__ldcg(scores + i));
   const int kvalid = min(kout, n);
   // The key prefix found so far, as its score half and its ~index half.
   uint32_t pre_hi = 0u, msk_hi = 0u, pre_lo = 0u, msk_lo = 0u;
   int need = kvalid;  // keys still wanted from the keys that match the prefix
   bool done = kvalid <= 0;
-#pragma unroll 1
-  for (int pass = 0; pass < 7; ++pass) {
-    if (done) break;
+  for (int pass = 0; pass < 7 && !done; ++pass) {
+    const bool hi = pass < 3;
     const int bits = pass < 2 ? 12 : 8;
     const int shift = pass == 0 ? 20 : pass == 1 ? 8 : pass == 2 ? 0 : 24 - 8 * (pass - 3);  // within its half
-    const bool hi = pass < 3;
     const int nb = 1 << bits;
     const int per = nb >= kThreads ? nb / kThreads : 1;
     for (int b = tid; b < nb; b += kThreads) s_hist[b] = 0u;
-    __syncthreads();
-#pragma unroll
-    for (int e = 0; e < kPer; ++e) {
-      const int i = e * kThreads + tid;
-      const uint32_t lo = ~static_cast<uint32_t>(i);
-      if (i < n && (sk[e] & msk_hi) == pre_hi && (lo & msk_lo) == pre_lo)
-        atomicAdd(&s_hist[((hi ? sk[e] : lo) >> shift) & uint32_t(nb - 1)], 1u);
+    __syncthreads();  // also orders the staging of s_sk before the first pass
+    if (hi) {
+      for (int i = tid; i < n; i += kThreads) {
+        const uint32_t k = s_sk[i];
+        if ((k & msk_hi) == pre_hi) atomicAdd(&s_hist[(k >> shift) & uint32_t(nb - 1)], 1u);
+      }
+    } else {  // the whole score half is fixed: only equal scores remain
+      for (int i = tid; i < n; i += kThreads) {
+        const uint32_t lo = ~static_cast<uint32_t>(i);
+        if (s_sk[i] == pre_hi && (lo & msk_lo) == pre_lo) atomicAdd(&s_hist[(lo >> shift) & 0xFFu], 1u);
+      }
     }
     __syncthreads();
     // Bins from the top: thread t owns bins nb-1-(t*per) down to nb-(t+1)*per.
@@ -176,37 +173,21 @@ __device__ void block_topk_radix(const float* scores, int n, int kout, int32_t* 
   if (tid == 0) s_misc[2] = 0u;
   __syncthreads();
   if (kvalid > 0) {
-#pragma unroll
-    for (int e = 0; e < kPer; ++e) {
-      const int i = e * kThreads + tid;
-      const unsigned long long k = (static_cast<unsigned long long>(sk[e]) << 32) | ~static_cast<uint32_t>(i);
-      if (i < n && k >= prefix) s_keys[atomicAdd(&s_misc[2], 1u)] = k;
+    for (int i = tid; i < n; i += kThreads) {
+      const unsigned long long k = (static_cast<unsigned long long>(s_sk[i]) << 32) | ~static_cast<uint32_t>(i);
+      if (k >= prefix) s_keys[atomicAdd(&s_misc[2], 1u)] = k;
     }
   }
   __syncthreads();
-  int m = 1;
-  while (m < kvalid) m <<= 1;
-  for (int i = kvalid + tid; i < m; i += kThreads) s_keys[i] = 0ull;
-  __syncthreads();
-  // Bitonic sort of s_keys[0, m), descending.
-  for (int size = 2; size <= m; size <<= 1) {
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      for (int i = tid; i < m; i += kThreads) {
-        const int j = i ^ stride;
-        if (j > i) {
-          const bool desc = (i & size) == 0;
-          const unsigned long long a = s_keys[i], b = s_keys[j];
-          if (desc ? a < b : a > b) {
-            s_keys[i] = b;
-            s_keys[j] = a;
-          }
-        }
-      }
-      __syncthreads();
-    }
+  // Each selected key's output position is the number of selected keys above
+  // it (all keys are distinct): one pass over s_keys, read as broadcasts.
+  if (tid < kvalid) {
+    const unsigned long long mine = s_keys[tid];
+    int rank = 0;
+    for (int j = 0; j < kvalid; ++j) rank += s_keys[j] > mine ? 1 : 0;
+    out[rank] = static_cast<int32_t>(~static_cast<unsigned>(mine & 0xffffffffull));
   }
-  for (int r = tid; r < kout; r += kThreads)
-    out[r] = r < kvalid ? static_cast<int32_t>(~static_cast<unsigned>(s_keys[r] & 0xffffffffull)) : -1;
+  for (int r = kvalid + tid; r < kout; r += kThreads) out[r] = -1;
 }
 
 }  // namespace topk

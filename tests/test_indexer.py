@@ -87,14 +87,14 @@ def test_indexer_matches_oracle(cuda, nq, n, top_k, ragged):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("nq,n,top_k", [(3, 16384, 512), (2, 16384, 64), (2, 20000, 64), (2, 3000, 600),
-                                        (2, 700, 700)])
+@pytest.mark.parametrize("nq,n,top_k", [(3, 16384, 512), (2, 16384, 64), (2, 20000, 64), (2, 49152, 100),
+                                        (1, 50000, 32), (2, 3000, 600), (2, 700, 700)])
 def test_indexer_ties_exact(cuda, nq, n, top_k):
     """Scores that are small integers (exact in fp32 whatever the summation
     order) with heavy ties: the selection must equal the oracle's bit for bit,
     equal scores ordered by the lower slot.  Covers the radix path (its index
-    digits are reached only through ties) and the per-round fallback (more
-    than 16384 slots, top_k above 512)."""
+    digits are reached only through ties) up to its 49152-slot limit and the
+    per-round fallback (more slots, or top_k above 512)."""
     from csahca_b200 import extension as ext
 
     rng = np.random.default_rng(n + top_k)
