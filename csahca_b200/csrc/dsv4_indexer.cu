@@ -235,13 +235,10 @@ constexpr int kTopkMaxSlots = 49152;  // radix path: the scores of one query sta
 // top_k <= 512.  Dynamic shared memory: n_keys words.
 __global__ void __launch_bounds__(kTopkThreads, 2) indexer_topk_kernel(IndexerParams p, int kout, int32_t* out) {
   extern __shared__ uint32_t s_sk[];
-  __shared__ unsigned s_hist[4096];
-  __shared__ unsigned s_wsum[kTopkThreads / 32];
-  __shared__ unsigned s_misc[4];
-  __shared__ unsigned long long s_keys[kTopkThreads];
+  __shared__ topk::RadixSmem<kTopkThreads> sm;
   const int qi = blockIdx.x;
   topk::block_topk_radix<kTopkThreads>(p.scores + size_t(qi) * p.n_keys, valid_slots(p, qi), kout,
-                                       out + size_t(qi) * kout, s_sk, s_hist, s_wsum, s_keys, s_misc);
+                                       out + size_t(qi) * kout, s_sk, sm);
 }
 
 // Same result for any n_keys and top_k, one selection round per output (leaves

@@ -78,113 +78,177 @@ namespace topk {
 // Top-k by radix selection, for kout <= kThreads.  Every element has the
 // unique 64-bit key (order-preserving score bits, ~index), so the k largest
 // keys are exactly the k largest scores with ties to the lower index.  The
-// score halves are staged once in shared memory (s_sk, n words); the index
-// half follows from the position.  Histogram passes over digits of 12, 12 and
-// 8 bits (then 8-bit digits of the index, reached only by equal scores) narrow
-// the key prefix; a pass whose chosen bin is wanted whole ends the search
-// early, since every key in it is then taken.  The keys at or above the final
-// prefix are compacted and each is written at its rank among them.  Same
-// results as block_topk.
-// Shared memory: s_sk n words, s_hist 4096 unsigned, s_wsum kThreads/32
-// unsigned, s_keys kThreads unsigned long long, s_misc 4 unsigned.
+// score halves are staged once in shared memory; the index half follows from
+// the position.
+//
+//   1. Staging and the histogram of the top 12 score bits in one pass.
+//   2. The bin holding the k-th largest key; if it is wanted whole, every key
+//      of the bins at or above it is taken and the search ends.
+//   3. Otherwise one pass splits the keys: those above the bin are taken,
+//      those in it (a few hundred for real score distributions) become
+//      candidates, and the remaining digits (12, 8 score bits, then 8-bit
+//      digits of the index, reached only by equal scores) are resolved over
+//      the candidates alone.  A bin with more than kRadixCand members is
+//      resolved by passes over all keys instead.
+//   4. Each taken key is written at its rank among the taken keys.
+// Same results as block_topk.
+constexpr int kRadixBins = 4096;
+constexpr int kRadixCand = 2048;
+
 template <int kThreads>
-__device__ void block_topk_radix(const float* scores, int n, int kout, int32_t* out, uint32_t* s_sk,
-                                 unsigned* s_hist, unsigned* s_wsum, unsigned long long* s_keys, unsigned* s_misc) {
+struct RadixSmem {
+  unsigned hist[kRadixBins];
+  unsigned wsum[32];
+  unsigned misc[8];  // bin, need, whole, taken count, candidate count
+  unsigned long long keys[kThreads];
+  uint32_t cand[kRadixCand];
+};
+
+// The bin (of nb, from the top) that holds the need-th largest counted key.
+// Each warp scans a contiguous run of bins, lanes on consecutive words.
+// Writes misc[0] = bin, misc[1] = keys still wanted inside it, misc[2] = 1 if
+// that is the whole bin.  Ends with a barrier.
+template <int kThreads>
+__device__ __forceinline__ void radix_find_bin(RadixSmem<kThreads>& sm, int nb, unsigned need) {
   constexpr int kWarps = kThreads / 32;
-  static_assert(kWarps <= 32 && kThreads % 32 == 0, "one warp scans the warp totals");
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  for (int i = tid; i < n; i += kThreads) s_sk[i] = float_order_key(__ldcg(scores + i));
-  const int kvalid = min(kout, n);
-  // The key prefix found so far, as its score half and its ~index half.
-  uint32_t pre_hi = 0u, msk_hi = 0u, pre_lo = 0u, msk_lo = 0u;
-  int need = kvalid;  // keys still wanted from the keys that match the prefix
-  bool done = kvalid <= 0;
-  for (int pass = 0; pass < 7 && !done; ++pass) {
-    const bool hi = pass < 3;
-    const int bits = pass < 2 ? 12 : 8;
-    const int shift = pass == 0 ? 20 : pass == 1 ? 8 : pass == 2 ? 0 : 24 - 8 * (pass - 3);  // within its half
-    const int nb = 1 << bits;
-    const int per = nb >= kThreads ? nb / kThreads : 1;
-    for (int b = tid; b < nb; b += kThreads) s_hist[b] = 0u;
-    __syncthreads();  // also orders the staging of s_sk before the first pass
-    if (hi) {
-      for (int i = tid; i < n; i += kThreads) {
-        const uint32_t k = s_sk[i];
-        if ((k & msk_hi) == pre_hi) atomicAdd(&s_hist[(k >> shift) & uint32_t(nb - 1)], 1u);
-      }
-    } else {  // the whole score half is fixed: only equal scores remain
-      for (int i = tid; i < n; i += kThreads) {
-        const uint32_t lo = ~static_cast<uint32_t>(i);
-        if (s_sk[i] == pre_hi && (lo & msk_lo) == pre_lo) atomicAdd(&s_hist[(lo >> shift) & 0xFFu], 1u);
-      }
-    }
-    __syncthreads();
-    // Bins from the top: thread t owns bins nb-1-(t*per) down to nb-(t+1)*per.
-    unsigned tot = 0;
-    const bool owns = tid * per < nb;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int seg = nb / kWarps;
+  const int top = nb - 1 - warp * seg;  // this warp's bins: top, top-1, ..., top-seg+1
+  unsigned t = 0;
+  for (int r = lane; r < seg; r += 32) t += sm.hist[top - r];
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      if (j < per && owns) tot += s_hist[nb - 1 - (tid * per + j)];
-    unsigned incl = tot;
+  for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+  if (lane == 0) sm.wsum[warp] = t;
+  __syncthreads();
+  if (warp == 0) {
+    const unsigned w = lane < kWarps ? sm.wsum[lane] : 0u;
+    unsigned wi = w;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const unsigned v = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += v;
+      const unsigned v = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += v;
     }
-    if (lane == 31) s_wsum[warp] = incl;
-    __syncthreads();
-    if (warp == 0) {
-      const unsigned w = lane < kWarps ? s_wsum[lane] : 0u;
-      unsigned wi = w;
+    __syncwarp();
+    if (lane < kWarps) sm.wsum[lane] = wi - w;  // keys in the bins above each warp's run
+  }
+  __syncthreads();
+  unsigned run = sm.wsum[warp];
+  if (run < need && run + t >= need) {  // the target bin is in this warp's run
+    for (int r0 = 0; r0 < seg; r0 += 32) {
+      const int r = r0 + lane;
+      const unsigned c = r < seg ? sm.hist[top - r] : 0u;
+      unsigned incl = c;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
-        const unsigned v = __shfl_up_sync(0xffffffffu, wi, o);
-        if (lane >= o) wi += v;
+        const unsigned v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
       }
-      __syncwarp();
-      if (lane < kWarps) s_wsum[lane] = wi - w;  // exclusive prefix of the warp totals
+      const unsigned before = run + incl - c;
+      if (r < seg && before < need && before + c >= need) {
+        sm.misc[0] = unsigned(top - r);
+        sm.misc[1] = need - before;
+        sm.misc[2] = before + c == need ? 1u : 0u;
+      }
+      run += __shfl_sync(0xffffffffu, incl, 31);
     }
-    __syncthreads();
-    unsigned run = s_wsum[warp] + incl - tot;
+  }
+  __syncthreads();
+}
+
+template <int kThreads>
+__device__ void block_topk_radix(const float* scores, int n, int kout, int32_t* out, uint32_t* s_sk,
+                                 RadixSmem<kThreads>& sm) {
+  static_assert(kThreads % 32 == 0 && kThreads / 32 <= 32 && kRadixBins % (kThreads / 32) == 0 &&
+                    256 % (kThreads / 32) == 0,
+                "warp-segmented bin scan");
+  const int tid = threadIdx.x;
+  const int kvalid = min(kout, n);
+  if (kvalid <= 0) {
+    for (int r = tid; r < kout; r += kThreads) out[r] = -1;
+    return;
+  }
+  // 1. Stage the order keys and count their top 12 bits.
+  for (int b = tid; b < kRadixBins; b += kThreads) sm.hist[b] = 0u;
+  if (tid == 0) sm.misc[3] = sm.misc[4] = 0u;
+  __syncthreads();
+  for (int base = 0; base < n; base += 8 * kThreads) {
+    float v[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      if (!(j < per && owns)) continue;
-      const unsigned c = s_hist[nb - 1 - (tid * per + j)];
-      if (run < unsigned(need) && run + c >= unsigned(need)) {
-        s_misc[0] = unsigned(nb - 1 - (tid * per + j));
-        s_misc[1] = unsigned(need) - run;
-        s_misc[3] = (run + c == unsigned(need)) ? 1u : 0u;
+    for (int e = 0; e < 8; ++e) {
+      const int i = base + e * kThreads + tid;
+      v[e] = i < n ? __ldcg(scores + i) : 0.f;
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int i = base + e * kThreads + tid;
+      if (i < n) {
+        const uint32_t k = float_order_key(v[e]);
+        s_sk[i] = k;
+        atomicAdd(&sm.hist[k >> 20], 1u);
       }
-      run += c;
+    }
+  }
+  __syncthreads();
+  // 2. The bin of the k-th largest key.
+  radix_find_bin(sm, kRadixBins, unsigned(kvalid));
+  const uint32_t bin0 = sm.misc[0];
+  unsigned need = sm.misc[1];
+  bool done = sm.misc[2] != 0u;
+  const bool use_cand = !done && sm.hist[bin0] <= unsigned(kRadixCand);
+  uint32_t pre_hi = bin0 << 20, msk_hi = 0xFFF00000u, pre_lo = 0u, msk_lo = 0u;
+  // 3. Split: keys above the bin are taken, the bin's keys become candidates.
+  if (use_cand) {
+    for (int i = tid; i < n; i += kThreads) {
+      const uint32_t k = s_sk[i];
+      const uint32_t b = k >> 20;
+      if (b > bin0)
+        sm.keys[atomicAdd(&sm.misc[3], 1u)] = (static_cast<unsigned long long>(k) << 32) | ~static_cast<uint32_t>(i);
+      else if (b == bin0)
+        sm.cand[atomicAdd(&sm.misc[4], 1u)] = uint32_t(i);
+    }
+  }
+  __syncthreads();
+  const int m = use_cand ? int(sm.misc[4]) : n;  // elements the remaining passes visit
+  for (int pass = 1; pass < 7 && !done; ++pass) {
+    const bool hi = pass < 3;
+    const int bits = pass == 1 ? 12 : 8;
+    const int shift = pass == 1 ? 8 : pass == 2 ? 0 : 24 - 8 * (pass - 3);  // within its half
+    const int nb = 1 << bits;
+    for (int b = tid; b < nb; b += kThreads) sm.hist[b] = 0u;
+    __syncthreads();
+    for (int c = tid; c < m; c += kThreads) {
+      const int i = use_cand ? int(sm.cand[c]) : c;
+      const uint32_t k = s_sk[i], lo = ~static_cast<uint32_t>(i);
+      if ((k & msk_hi) == pre_hi && (lo & msk_lo) == pre_lo)
+        atomicAdd(&sm.hist[((hi ? k : lo) >> shift) & uint32_t(nb - 1)], 1u);
     }
     __syncthreads();
+    radix_find_bin(sm, nb, need);
     if (hi) {
-      pre_hi |= s_misc[0] << shift;
+      pre_hi |= sm.misc[0] << shift;
       msk_hi |= uint32_t(nb - 1) << shift;
     } else {
-      pre_lo |= s_misc[0] << shift;
+      pre_lo |= sm.misc[0] << shift;
       msk_lo |= uint32_t(nb - 1) << shift;
     }
-    need = int(s_misc[1]);
-    done = s_misc[3] != 0u;
+    need = sm.misc[1];
+    done = sm.misc[2] != 0u;
   }
-  // Exactly kvalid keys are >= the prefix (lower bits zero when the search ended early).
+  // Every key >= the prefix (lower bits zero when the search ended early) is
+  // taken: kvalid keys with those already taken in step 3.
   const unsigned long long prefix = (static_cast<unsigned long long>(pre_hi) << 32) | pre_lo;
-  if (tid == 0) s_misc[2] = 0u;
-  __syncthreads();
-  if (kvalid > 0) {
-    for (int i = tid; i < n; i += kThreads) {
-      const unsigned long long k = (static_cast<unsigned long long>(s_sk[i]) << 32) | ~static_cast<uint32_t>(i);
-      if (k >= prefix) s_keys[atomicAdd(&s_misc[2], 1u)] = k;
-    }
+  for (int c = tid; c < m; c += kThreads) {
+    const int i = use_cand ? int(sm.cand[c]) : c;
+    const unsigned long long k = (static_cast<unsigned long long>(s_sk[i]) << 32) | ~static_cast<uint32_t>(i);
+    if (k >= prefix) sm.keys[atomicAdd(&sm.misc[3], 1u)] = k;
   }
   __syncthreads();
-  // Each selected key's output position is the number of selected keys above
-  // it (all keys are distinct): one pass over s_keys, read as broadcasts.
+  // 4. Each taken key's output position is the number of taken keys above it.
   if (tid < kvalid) {
-    const unsigned long long mine = s_keys[tid];
+    const unsigned long long mine = sm.keys[tid];
     int rank = 0;
-    for (int j = 0; j < kvalid; ++j) rank += s_keys[j] > mine ? 1 : 0;
+#pragma unroll 4
+    for (int j = 0; j < kvalid; ++j) rank += sm.keys[j] > mine ? 1 : 0;
     out[rank] = static_cast<int32_t>(~static_cast<unsigned>(mine & 0xffffffffull));
   }
   for (int r = kvalid + tid; r < kout; r += kThreads) out[r] = -1;
