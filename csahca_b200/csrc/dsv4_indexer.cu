@@ -232,9 +232,9 @@ constexpr int kTopkMaxSlots = 49152;  // radix path: the scores of one query sta
 
 // Top-k of query blockIdx.x's valid scores (largest first, ties to the lower
 // slot, -1 past the valid count), by radix selection: n_keys <= 49152 and
-// top_k <= 512.  Dynamic shared memory: n_keys words.
+// top_k <= 512.  Dynamic shared memory: n_keys words rounded up to a multiple of 4.
 __global__ void __launch_bounds__(kTopkThreads, 2) indexer_topk_kernel(IndexerParams p, int kout, int32_t* out) {
-  extern __shared__ uint32_t s_sk[];
+  extern __shared__ __align__(16) uint32_t s_sk[];
   __shared__ topk::RadixSmem<kTopkThreads> sm;
   const int qi = blockIdx.x;
   topk::block_topk_radix<kTopkThreads>(p.scores + size_t(qi) * p.n_keys, valid_slots(p, qi), kout,
@@ -300,7 +300,8 @@ extern "C" int csahca_dsv4_indexer_topk(const void* q, const float* weights, con
   indexer_score_kernel<<<grid, kThreads, kSmemBytes, s>>>(p);
   CSAHCA_RETURN_IF_CUDA(cudaGetLastError());
   if (n_keys <= kTopkMaxSlots && kout <= kTopkThreads)
-    indexer_topk_kernel<<<unsigned(num_queries), kTopkThreads, size_t(n_keys) * 4, s>>>(p, int(kout), out_indices);
+    indexer_topk_kernel<<<unsigned(num_queries), kTopkThreads, size_t((n_keys + 3) & ~int64_t(3)) * 4, s>>>(
+        p, int(kout), out_indices);  // whole 16-byte groups: the split pass reads four keys at a time
   else
     indexer_topk_rounds_kernel<<<unsigned(num_queries), kTopkThreads, 0, s>>>(p, int(kout), out_indices);
   CSAHCA_RETURN_IF_CUDA(cudaGetLastError());
