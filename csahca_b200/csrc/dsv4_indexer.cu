@@ -65,6 +65,7 @@ struct IndexerParams {
   const int32_t* lens;     // [Q] valid slots (nullptr: all N)
   float* scores;           // [Q, N]
   int num_queries, n_keys;
+  int tiles_per_cta;       // 128-slot tiles one CTA streams
   int* err;
 };
 
@@ -93,8 +94,8 @@ __global__ void __launch_bounds__(kThreads, 2) indexer_score_kernel(IndexerParam
   volatile int* abort_flag = &bars->abort_flag;
   const int qi = blockIdx.y;
   const int n = valid_slots(p, qi);
-  const int tile0 = blockIdx.x * kTilesPerCta;
-  const int ntiles = max(0, min(kTilesPerCta, (n + kTile - 1) / kTile - tile0));
+  const int tile0 = blockIdx.x * p.tiles_per_cta;
+  const int ntiles = max(0, min(p.tiles_per_cta, (n + kTile - 1) / kTile - tile0));
   if (ntiles == 0) return;  // uniform across the CTA, before any barrier
 
   if (threadIdx.x == 0) {
@@ -296,6 +297,7 @@ extern "C" int csahca_dsv4_indexer_topk(const void* q, const float* weights, con
     configured[dev] = true;
   }
   const int tiles = int((n_keys + kTile - 1) / kTile);
+  p.tiles_per_cta = kTilesPerCta;  // 8, 24, 32, 64 and 128 measured slower at 32-256 queries
   const dim3 grid(unsigned((tiles + kTilesPerCta - 1) / kTilesPerCta), unsigned(num_queries));
   indexer_score_kernel<<<grid, kThreads, kSmemBytes, s>>>(p);
   CSAHCA_RETURN_IF_CUDA(cudaGetLastError());
