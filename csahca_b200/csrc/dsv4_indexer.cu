@@ -12,14 +12,15 @@
 // indexer key per compressed slot s), then the top-k slots by I (largest
 // first, equal scores by lower slot, -1 past the valid count).
 //
-// Score kernel: one CTA per (query, run of 128-slot tiles).  Per tile,
+// Score kernel: persistent, two CTAs per SM, each streaming an equal share
+// of all queries' 128-slot tiles.  Per tile,
 //   S^T[slot, head] = K[slot, :] . Q[head, :]       (M=128 slots, N=H heads, K=D)
 // runs as tcgen05.mma kind::f16 (bf16 in, fp32 accumulate in TMEM); each of
 // 128 epilogue threads owns one slot (TMEM lane) and reduces its row with the
 // weights and the ReLU.  Four producer warps copy the key tiles (rows of D
 // bf16, 256 B for D = 128) into 128-byte-swizzled shared memory with cp.async,
-// two tiles in flight.  Top-k kernel: one 1024-thread CTA per query over the
-// stored scores (the block top-k shared with the CSA scorers).
+// two tiles in flight.  Top-k kernel: one 512-thread CTA per query, radix
+// selection over the stored scores (topk.cuh).
 #include <algorithm>
 
 #include "common.cuh"
@@ -39,24 +40,25 @@ constexpr int kProdWarp0 = 4;
 constexpr int kProdWarps = 4;
 constexpr int kMmaWarp = kProdWarp0 + kProdWarps;
 constexpr int kThreads = (kMmaWarp + 1) * 32;  // 288
-constexpr int kTilesPerCta = 16;
 
 constexpr uint32_t kSubBytes = kTile * 128;                 // 16 KB: 128 slots x 64 dims
 constexpr uint32_t kKTileBytes = 2 * kSubBytes;             // 32 KB
 constexpr uint32_t kQSubBytes = kIdxHeads * 128;            // 8 KB: 64 heads x 64 dims
-constexpr uint32_t kOffQ = 0;
-constexpr uint32_t kOffK = kOffQ + 2 * kQSubBytes;
+constexpr uint32_t kQBytes = 2 * kQSubBytes;                // 16 KB: one query's indexer q
+constexpr uint32_t kOffQ = 0;                               // two Q buffers
+constexpr uint32_t kOffK = kOffQ + 2 * kQBytes;             // two key tiles
 constexpr uint32_t kOffBar = kOffK + 2 * kKTileBytes;
-constexpr uint32_t kSmemBytes = kOffBar + 1024 + 1024;      // barriers, weights + alignment slack
+constexpr uint32_t kSmemBytes = kOffBar + 2048 + 1024;      // barriers and weights + alignment slack
 constexpr uint32_t kTmemCols = 128;                         // two S^T buffers of 64 columns
 constexpr uint32_t kIdesc = idesc_bf16_f32(kTile, kIdxHeads, 0, 0);
 
 struct IdxBars {
-  uint64_t k_full[2], k_empty[2], s_full[2], s_empty[2];
+  uint64_t k_full[2], k_empty[2], s_full[2], s_empty[2], q_empty[2];
   uint32_t tmem_base;
   int abort_flag;
-  float w[kIdxHeads];
+  float w[kEpiWarps][kIdxHeads];  // each epilogue warp's copy of the current query's weights
 };
+static_assert(sizeof(IdxBars) <= 2048, "barrier region");
 
 struct IndexerParams {
   const __nv_bfloat16* q;  // [Q, H, D]
@@ -65,7 +67,7 @@ struct IndexerParams {
   const int32_t* lens;     // [Q] valid slots (nullptr: all N)
   float* scores;           // [Q, N]
   int num_queries, n_keys;
-  int tiles_per_cta;       // 128-slot tiles one CTA streams
+  int tiles_per_query;     // ceil(n_keys / 128)
   int* err;
 };
 
@@ -82,9 +84,29 @@ __device__ __forceinline__ uint32_t sw128(int row, int c16) {
 }
 
 __device__ __forceinline__ int valid_slots(const IndexerParams& p, int q) {
-  return p.lens != nullptr ? max(0, min(p.lens[q], p.n_keys)) : p.n_keys;
+  return p.lens != nullptr ? max(0, min(__ldg(p.lens + q), p.n_keys)) : p.n_keys;
 }
 
+// The tiles of all queries in one sequence, query-major: tile g is tile
+// g % T of query g / T.  A tile at or past the query's valid count holds no
+// work; every role skips it the same way.
+struct TileRef {
+  int q, t, n;
+};
+__device__ __forceinline__ bool tile_at(const IndexerParams& p, int g, TileRef& r) {
+  r.q = g / p.tiles_per_query;
+  r.t = g - r.q * p.tiles_per_query;
+  r.n = valid_slots(p, r.q);
+  return r.t * kTile < r.n;
+}
+
+// Persistent: CTA c streams the tiles [total*c/G, total*(c+1)/G) of the
+// sequence, so every CTA gets the same number of tiles whatever the number of
+// queries (no partial last wave).  A range crosses query boundaries: each
+// query it touches is a "visit" v, whose q goes to Q buffer v % 2, loaded in
+// the same cp.async group as the visit's first key tile (so that tile's
+// k_full also publishes q); the MMA thread frees the buffer with a commit
+// after the visit's last tile.
 __global__ void __launch_bounds__(kThreads, 2) indexer_score_kernel(IndexerParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -92,11 +114,9 @@ __global__ void __launch_bounds__(kThreads, 2) indexer_score_kernel(IndexerParam
   const uint32_t q_base = smem_u32(smem + kOffQ), k_base = smem_u32(smem + kOffK);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   volatile int* abort_flag = &bars->abort_flag;
-  const int qi = blockIdx.y;
-  const int n = valid_slots(p, qi);
-  const int tile0 = blockIdx.x * p.tiles_per_cta;
-  const int ntiles = max(0, min(p.tiles_per_cta, (n + kTile - 1) / kTile - tile0));
-  if (ntiles == 0) return;  // uniform across the CTA, before any barrier
+  // total < 2^31 / 128: the host caps num_queries * n_keys at 2^31.
+  const long long total = (long long)p.num_queries * p.tiles_per_query;
+  const int g0 = int(total * blockIdx.x / gridDim.x), g1 = int(total * (blockIdx.x + 1) / gridDim.x);
 
   if (threadIdx.x == 0) {
     for (int b = 0; b < 2; ++b) {
@@ -104,11 +124,11 @@ __global__ void __launch_bounds__(kThreads, 2) indexer_score_kernel(IndexerParam
       mbar_init(&bars->k_empty[b], 1);
       mbar_init(&bars->s_full[b], 1);
       mbar_init(&bars->s_empty[b], kEpiWarps * 32);
+      mbar_init(&bars->q_empty[b], 1);
     }
     bars->abort_flag = 0;
     fence_mbar_init();
   }
-  if (threadIdx.x < kIdxHeads) bars->w[threadIdx.x] = p.w[size_t(qi) * kIdxHeads + threadIdx.x];
   if (warp == kMmaWarp) tmem_alloc(&bars->tmem_base, kTmemCols);
   tc_fence_before();
   __syncthreads();
@@ -118,81 +138,115 @@ __global__ void __launch_bounds__(kThreads, 2) indexer_score_kernel(IndexerParam
 
   if (warp >= kProdWarp0 && warp < kProdWarp0 + kProdWarps) {
     // ------------------------------------------------------------ producers
-    // Chunk c (16 B) of a 256-byte key row goes to sub-tile c/8, swizzled
-    // chunk c%8 of the row; Q row pt/2 half pt%2 is copied once.  Rows past
-    // the valid count are zero-filled.
+    // Key tiles: 16 consecutive threads copy one 256-byte row (chunk c = pt %
+    // 16, sub-tile c / 8, swizzled chunk c % 8), so every warp instruction
+    // reads 512 contiguous bytes; rows past the valid count are zero-filled.
+    // q: thread pt copies head pt / 2, half pt % 2.
     const int pt = threadIdx.x - kProdWarp0 * 32;
-    {
-      const int head = pt >> 1, half = pt & 1;
-      const __nv_bfloat16* src = p.q + (size_t(qi) * kIdxHeads + head) * kIdxDim + half * 64;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) cp_async16(q_base + uint32_t(half) * kQSubBytes + sw128(head, c), src + c * 8);
-    }
-    const __nv_bfloat16* kq = p.k + size_t(qi) * p.n_keys * kIdxDim;
-    // Key tiles: 16 consecutive threads copy one 256-byte row (chunk c = pt % 16),
-    // so every warp instruction reads 512 contiguous bytes.
     const int c = pt & 15, r0 = pt >> 4;  // rows r0, r0 + 8, ..., r0 + 120
     const uint32_t c_off = uint32_t(c >> 3) * kSubBytes;
     bool ok = true;
-    for (int i = 0; i < ntiles && ok; ++i) {
+    int i = 0, v = -1, prev_q = -1;
+    for (int g = g0; g < g1 && ok; ++g) {
+      TileRef tr;
+      if (!tile_at(p, g, tr)) continue;
       const int b = i & 1;
       if (i >= 2) ok = mbar_wait(&bars->k_empty[b], ((i >> 1) - 1) & 1, abort_flag);
       if (!ok) break;
-      const int tile_slot = (tile0 + i) * kTile;
+      if (tr.q != prev_q) {
+        ++v;
+        prev_q = tr.q;
+        if (v >= 2) ok = mbar_wait(&bars->q_empty[v & 1], ((v >> 1) - 1) & 1, abort_flag);
+        if (!ok) break;
+        const int head = pt >> 1, half = pt & 1;
+        const __nv_bfloat16* src = p.q + (size_t(tr.q) * kIdxHeads + head) * kIdxDim + half * 64;
+        const uint32_t qd = q_base + uint32_t(v & 1) * kQBytes + uint32_t(half) * kQSubBytes;
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) cp_async16(qd + sw128(head, cc), src + cc * 8);
+      }
+      const __nv_bfloat16* kq = p.k + size_t(tr.q) * p.n_keys * kIdxDim;
+      const int tile_slot = tr.t * kTile;
       const uint32_t dst = k_base + uint32_t(b) * kKTileBytes + c_off;
 #pragma unroll
       for (int j = 0; j < kTile / 8; ++j) {
         const int row = r0 + 8 * j;
         const uint32_t a = dst + sw128(row, c & 7);
-        if (tile_slot + row < n)
+        if (tile_slot + row < tr.n)
           cp_async16(a, kq + size_t(tile_slot + row) * kIdxDim + c * 8);
         else
           asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(a), "r"(0u) : "memory");
       }
       cp_async_commit();
-      // The previous tile (and, with the first tile, Q) has landed: publish it.
+      // The previous tile (with its visit's q) has landed: publish it.
       if (i > 0) {
         cp_async_wait<1>();
         fence_proxy_async_smem();
         mbar_arrive(&bars->k_full[(i - 1) & 1]);
       }
+      ++i;
     }
-    if (ok) {
+    if (ok && i > 0) {
       cp_async_wait<0>();
       fence_proxy_async_smem();
-      mbar_arrive(&bars->k_full[(ntiles - 1) & 1]);
-    } else {
-      failed = true;
+      mbar_arrive(&bars->k_full[(i - 1) & 1]);
     }
+    if (!ok) failed = true;
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       bool ok = true;
-      for (int i = 0; i < ntiles && ok; ++i) {
+      int i = 0, v = -1, prev_q = -1;
+      for (int g = g0; g < g1 && ok; ++g) {
+        TileRef tr;
+        if (!tile_at(p, g, tr)) continue;
+        if (tr.q != prev_q) {
+          ++v;
+          prev_q = tr.q;
+        }
         const int b = i & 1;
         ok = mbar_wait(&bars->k_full[b], (i >> 1) & 1, abort_flag);
         if (ok && i >= 2) ok = mbar_wait(&bars->s_empty[b], ((i >> 1) - 1) & 1, abort_flag);
         if (!ok) break;
         tc_fence_after();
         const uint32_t kt = k_base + uint32_t(b) * kKTileBytes;
+        const uint32_t qt = q_base + uint32_t(v & 1) * kQBytes;
 #pragma unroll
         for (int kk = 0; kk < kIdxDim / 16; ++kk) {
           const uint32_t sub = uint32_t(kk >> 2), off = uint32_t(kk & 3) * 32u;
           mma_bf16_ss(tmem + 64 * b, smem_desc_sw128(kt + sub * kSubBytes + off, 16, 1024),
-                      smem_desc_sw128(q_base + sub * kQSubBytes + off, 16, 1024), kIdesc, kk != 0);
+                      smem_desc_sw128(qt + sub * kQSubBytes + off, 16, 1024), kIdesc, kk != 0);
         }
         mma_commit(&bars->s_full[b]);
         mma_commit(&bars->k_empty[b]);
+        // Last tile of this visit (the next tile with work is another query's,
+        // or there is none): its q buffer is free once these MMAs complete.
+        int gn = g + 1;
+        TileRef tn;
+        while (gn < g1 && !tile_at(p, gn, tn)) ++gn;
+        if (gn >= g1 || tn.q != tr.q) mma_commit(&bars->q_empty[v & 1]);
+        ++i;
       }
       if (!ok) failed = true;
     }
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue: one slot per thread
+    // At each visit's first tile every epilogue warp copies the query's
+    // weights into its own buffer (no barrier across warps).
     const int t = threadIdx.x;
     const uint32_t t_lane = tmem + (uint32_t(warp * 32) << 16);
-    float* out = p.scores + size_t(qi) * p.n_keys;
-    for (int i = 0; i < ntiles; ++i) {
+    float* w = bars->w[warp];
+    int i = 0, prev_q = -1;
+    for (int g = g0; g < g1; ++g) {
+      TileRef tr;
+      if (!tile_at(p, g, tr)) continue;
+      if (tr.q != prev_q) {
+        prev_q = tr.q;
+        __syncwarp();  // every lane is done with the previous query's weights
+        w[lane] = __ldg(p.w + size_t(tr.q) * kIdxHeads + lane);
+        w[lane + 32] = __ldg(p.w + size_t(tr.q) * kIdxHeads + lane + 32);
+        __syncwarp();
+      }
       const int b = i & 1;
       const bool ok = mbar_wait(&bars->s_full[b], (i >> 1) & 1, abort_flag);
       if (!ok) {
@@ -200,19 +254,20 @@ __global__ void __launch_bounds__(kThreads, 2) indexer_score_kernel(IndexerParam
         break;
       }
       tc_fence_after();
-      float v[32];
+      float sv[32];
       float acc = 0.f;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        tmem_ld32(t_lane + 64 * b + 32 * h, v);
+        tmem_ld32(t_lane + 64 * b + 32 * h, sv);
         tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < 32; ++c) acc = fmaf(bars->w[32 * h + c], fmaxf(v[c], 0.f), acc);
+        for (int c = 0; c < 32; ++c) acc = fmaf(w[32 * h + c], fmaxf(sv[c], 0.f), acc);
       }
       tc_fence_before();
       mbar_arrive(&bars->s_empty[b]);
-      const int slot = (tile0 + i) * kTile + t;
-      if (slot < n) out[slot] = acc;
+      const int slot = tr.t * kTile + t;
+      if (slot < tr.n) p.scores[size_t(tr.q) * p.n_keys + slot] = acc;
+      ++i;
     }
   }
   if (failed) {
@@ -274,8 +329,8 @@ extern "C" int csahca_dsv4_indexer_topk(const void* q, const float* weights, con
   if (n_keys * num_queries > (int64_t(1) << 31)) return csahca_set_unsupported("problem too large");
   if (workspace_bytes < csahca_dsv4_indexer_workspace_size(num_queries, n_keys))
     return csahca_set_arg_error("workspace too small");
-  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(keys)) & 15)
-    return csahca_set_arg_error("q and keys must be 16-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(keys) | reinterpret_cast<uintptr_t>(weights)) & 15)
+    return csahca_set_arg_error("q, weights and keys must be 16-byte aligned");
   IndexerParams p;
   p.q = static_cast<const __nv_bfloat16*>(q);
   p.w = weights;
@@ -287,18 +342,24 @@ extern "C" int csahca_dsv4_indexer_topk(const void* q, const float* weights, con
   p.err = csahca_device_error_ptr();
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   static bool configured[64] = {};
+  static int sm_count[64] = {};
   int dev = 0;
   CSAHCA_RETURN_IF_CUDA(cudaGetDevice(&dev));
   if (dev < 64 && !configured[dev]) {
+    CSAHCA_RETURN_IF_CUDA(cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev));
     CSAHCA_RETURN_IF_CUDA(
         cudaFuncSetAttribute(indexer_score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes)));
     CSAHCA_RETURN_IF_CUDA(cudaFuncSetAttribute(indexer_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                kTopkMaxSlots * 4));
     configured[dev] = true;
   }
-  const int tiles = int((n_keys + kTile - 1) / kTile);
-  p.tiles_per_cta = kTilesPerCta;  // 8, 24, 32, 64 and 128 measured slower at 32-256 queries
-  const dim3 grid(unsigned((tiles + kTilesPerCta - 1) / kTilesPerCta), unsigned(num_queries));
+  p.tiles_per_query = int((n_keys + kTile - 1) / kTile);
+  int sms = dev < 64 ? sm_count[dev] : 0;
+  if (sms <= 0) CSAHCA_RETURN_IF_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  // Persistent: two CTAs per SM (96 registers, ~99 KB of shared memory each),
+  // each streaming an equal share of all queries' tiles.
+  const int64_t total_tiles = num_queries * int64_t(p.tiles_per_query);
+  const unsigned grid = unsigned(std::min<int64_t>(total_tiles, int64_t(2) * sms));
   indexer_score_kernel<<<grid, kThreads, kSmemBytes, s>>>(p);
   CSAHCA_RETURN_IF_CUDA(cudaGetLastError());
   if (n_keys <= kTopkMaxSlots && kout <= kTopkThreads)
