@@ -113,6 +113,25 @@ def test_indexer_ties_exact(cuda, nq, n, top_k):
 
 
 @pytest.mark.gpu
+def test_indexer_bench_batch(cuda):
+    """The bench's own full batch (config 5's shape: 256 queries x 16384 C4
+    slots, generated exactly as ``bench.py --workload dsv4_indexer`` does,
+    top-64): a spread of queries checked against the oracle with the same
+    per-position contract."""
+    from csahca_b200 import extension as ext
+    from helpers import to_numpy
+
+    g = torch.Generator(device=cuda).manual_seed(5)
+    q = torch.randn(256, 64, 128, generator=g, device=cuda).to(torch.bfloat16)
+    w = torch.randn(256, 64, generator=g, device=cuda) * 0.1
+    keys = torch.randn(256, 16384, 128, generator=g, device=cuda, dtype=torch.bfloat16)
+    sel = ext.dsv4_indexer_topk(q, w, keys, 64).cpu().numpy()
+    pick = [0, 1, 37, 128, 147, 148, 200, 255]  # score-CTA tile shares cross query boundaries throughout
+    share = _check(sel[pick], to_numpy(q[pick]), w[pick].cpu().numpy(), to_numpy(keys[pick]), 64, None)
+    assert share > 0.9
+
+
+@pytest.mark.gpu
 def test_indexer_rejects_unsupported_shapes(cuda):
     from csahca_b200 import extension as ext
 
