@@ -114,7 +114,7 @@ __global__ void __launch_bounds__(kThreads, 2) indexer_score_kernel(IndexerParam
   const uint32_t q_base = smem_u32(smem + kOffQ), k_base = smem_u32(smem + kOffK);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   volatile int* abort_flag = &bars->abort_flag;
-  // total < 2^31 / 128: the host caps num_queries * n_keys at 2^31.
+  // total fits an int: the host requires num_queries * n_keys < 2^31.
   const long long total = (long long)p.num_queries * p.tiles_per_query;
   const int g0 = int(total * blockIdx.x / gridDim.x), g1 = int(total * (blockIdx.x + 1) / gridDim.x);
 
@@ -325,8 +325,7 @@ extern "C" int csahca_dsv4_indexer_topk(const void* q, const float* weights, con
   if (num_queries < 0 || n_keys < 0 || top_k <= 0) return csahca_set_arg_error("sizes must be non-negative, top_k positive");
   const int64_t kout = std::min<int64_t>(top_k, n_keys);
   if (num_queries == 0 || kout == 0) return CSAHCA_OK;
-  if (num_queries > 65535) return csahca_set_unsupported("at most 65535 queries per call");
-  if (n_keys * num_queries > (int64_t(1) << 31)) return csahca_set_unsupported("problem too large");
+  if (n_keys * num_queries >= (int64_t(1) << 31)) return csahca_set_unsupported("problem too large");
   if (workspace_bytes < csahca_dsv4_indexer_workspace_size(num_queries, n_keys))
     return csahca_set_arg_error("workspace too small");
   if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(keys) | reinterpret_cast<uintptr_t>(weights)) & 15)

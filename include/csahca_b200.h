@@ -162,7 +162,7 @@ int csahca_csa_decode_noalloc(const void* q, const void* k_cache, const void* v_
  * out_indices [Q, min(top_k, n_keys)] int32.  workspace:
  * csahca_dsv4_indexer_workspace_size() bytes of any content.  q, weights and
  * keys must be 16-byte aligned (CSAHCA_EINVAL otherwise); 64 heads of dim
- * 128 only, at most 65535 queries and num_queries * n_keys <= 2^31
+ * 128 only, num_queries * n_keys < 2^31
  * (CSAHCA_EUNSUPPORTED otherwise).
  */
 size_t csahca_dsv4_indexer_workspace_size(int64_t num_queries, int64_t n_keys);
